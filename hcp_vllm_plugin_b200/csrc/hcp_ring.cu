@@ -1,0 +1,330 @@
+// libhcp_ring.so: the C ABI declared in include/hcp_ring.h.
+//
+// Host side of the library: argument validation, TMA tensor-map encoding,
+// work scheduling (heaviest query tiles first, GQA heads of one KV head on
+// neighbouring CTAs) and kernel launches.  All kernels live in this single
+// translation unit so they share one device status word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "hcp_ring.h"
+#include "merge.cuh"
+#include "ring_fwd.cuh"
+
+namespace hcp {
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 128-byte-swizzled tiled map over a 16-bit tensor.  dims/box innermost first;
+// strides (bytes) for dims 1..rank-1.
+bool encode_map(CUtensorMap* m, bool f16, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t e[5] = {1, 1, 1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) s[i] = strides[i];
+  const CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, e,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// [rows, heads, D] view with the given row stride (elements).
+bool encode_rows_heads(CUtensorMap* m, bool f16, const void* base, int64_t rows, int heads, int D,
+                       int64_t row_stride) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(heads),
+                            static_cast<uint64_t>(std::max<int64_t>(rows, 1))};
+  const uint64_t strides[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(row_stride) * 2};
+  const uint32_t box[3] = {64, 1, 128};
+  return encode_map(m, f16, 3, base, dims, strides, box);
+}
+
+std::mutex g_attr_mu;
+bool g_attr_done[2][2][64];
+
+template <int D, bool F16>
+int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
+  constexpr int smem = fwd_smem_bytes<D>();
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    bool& done = g_attr_done[D == 128][F16][dev];
+    if (!done) {
+      if (cudaFuncSetAttribute(ring_fwd_kernel<D, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return HCP_ERR_CUDA;
+      done = true;
+    }
+  }
+  ring_fwd_kernel<D, F16><<<grid, kThreads, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
+int64_t segment_cost(const hcp_kv_segment& s, int q_len) {
+  if (s.src == HCP_SRC_NONE || s.len <= 0) return 0;
+  if (s.causal_off < 0) return static_cast<int64_t>(s.len) * q_len;
+  // average visible keys over the rows
+  const int64_t first = std::min<int64_t>(s.len, s.causal_off + 1);
+  const int64_t last = std::min<int64_t>(s.len, static_cast<int64_t>(s.causal_off) + q_len);
+  return (first + last) * q_len / 2;
+}
+
+int validate_segment(const hcp_fwd_args* a, const hcp_attn_work& w, const hcp_kv_segment& s) {
+  if (s.src == HCP_SRC_NONE || s.len == 0) return HCP_OK;
+  if (s.len < 0 || s.start < 0) return HCP_ERR_INVALID;
+  switch (s.src) {
+    case HCP_SRC_A:
+      if (a->k_a == nullptr || a->v_a == nullptr) return HCP_ERR_INVALID;
+      if (static_cast<int64_t>(s.start) + s.len > a->rows_a) return HCP_ERR_INVALID;
+      return HCP_OK;
+    case HCP_SRC_B:
+      if (a->k_b == nullptr || a->v_b == nullptr) return HCP_ERR_INVALID;
+      if (static_cast<int64_t>(s.start) + s.len > a->rows_b) return HCP_ERR_INVALID;
+      return HCP_OK;
+    case HCP_SRC_PAGED:
+      if (a->kv_cache == nullptr || a->block_table == nullptr) return HCP_ERR_INVALID;
+      if (w.paged_req < 0 || w.paged_req >= a->block_table_rows) return HCP_ERR_INVALID;
+      if (s.start % a->block_size != 0) return HCP_ERR_UNSUPPORTED;
+      if (static_cast<int64_t>(s.start) + s.len > a->block_table_stride * a->block_size)
+        return HCP_ERR_INVALID;
+      return HCP_OK;
+    default:
+      return HCP_ERR_INVALID;
+  }
+}
+
+}  // namespace
+}  // namespace hcp
+
+using namespace hcp;
+
+extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
+  if (a == nullptr) return HCP_ERR_INVALID;
+  if (a->dtype != HCP_BF16 && a->dtype != HCP_F16) return HCP_ERR_UNSUPPORTED;
+  const bool f16 = a->dtype == HCP_F16;
+  const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim;
+  if (H <= 0 || Hkv <= 0 || H % Hkv != 0) return HCP_ERR_INVALID;
+  if (D != 64 && D != 128) return HCP_ERR_UNSUPPORTED;
+  if (!(a->scale > 0.f) || !std::isfinite(a->scale)) return HCP_ERR_INVALID;
+  if (a->num_work < 0 || (a->num_work > 0 && a->work == nullptr)) return HCP_ERR_INVALID;
+  if (a->q == nullptr || a->out == nullptr || a->q_rows < 0) return HCP_ERR_INVALID;
+  if (a->q_row_stride < static_cast<int64_t>(H) * D || a->out_row_stride < static_cast<int64_t>(H) * D)
+    return HCP_ERR_INVALID;
+  if (a->out_dtype != a->dtype && a->out_dtype != HCP_F32) return HCP_ERR_UNSUPPORTED;
+  if (!aligned16(a->q) || !aligned16(a->out) || (a->q_row_stride % 8) != 0 ||
+      (a->out_row_stride % 8) != 0)
+    return HCP_ERR_INVALID;
+  if (a->merge_lse != nullptr) {
+    if (a->merge_o == nullptr || !aligned16(a->merge_o)) return HCP_ERR_INVALID;
+    if (a->merge_o_dtype != a->dtype && a->merge_o_dtype != HCP_F32) return HCP_ERR_UNSUPPORTED;
+    if (a->merge_o_row_stride < static_cast<int64_t>(H) * D || (a->merge_o_row_stride % 8) != 0)
+      return HCP_ERR_INVALID;
+  }
+  const bool want_a = a->k_a != nullptr, want_b = a->k_b != nullptr, want_paged = a->kv_cache != nullptr;
+  const int64_t kv_row = static_cast<int64_t>(Hkv) * D;
+  if (want_a && (a->v_a == nullptr || a->rows_a <= 0 || a->a_row_stride < kv_row ||
+                 (a->a_row_stride % 8) != 0 || !aligned16(a->k_a) || !aligned16(a->v_a)))
+    return HCP_ERR_INVALID;
+  if (want_b && (a->v_b == nullptr || a->rows_b <= 0 || a->b_row_stride < kv_row ||
+                 (a->b_row_stride % 8) != 0 || !aligned16(a->k_b) || !aligned16(a->v_b)))
+    return HCP_ERR_INVALID;
+  if (want_paged) {
+    const int bs = a->block_size;
+    if (bs != 16 && bs != 32 && bs != 64 && bs != 128) return HCP_ERR_UNSUPPORTED;
+    if (a->num_blocks <= 0 || a->num_blocks >= (1ll << 31) || a->block_table == nullptr ||
+        a->block_table_stride <= 0 || a->block_table_rows <= 0 || !aligned16(a->kv_cache))
+      return HCP_ERR_INVALID;
+  }
+
+  // Validate and order the work: most expensive items first.
+  std::vector<hcp_attn_work> items;
+  items.reserve(a->num_work);
+  std::vector<int64_t> cost;
+  for (int i = 0; i < a->num_work; ++i) {
+    const hcp_attn_work& w = a->work[i];
+    if (w.q_len < 0 || w.q_start < 0 || static_cast<int64_t>(w.q_start) + w.q_len > a->q_rows)
+      return HCP_ERR_INVALID;
+    if (a->lse != nullptr && (w.lse_col < 0 || static_cast<int64_t>(w.lse_col) + w.q_len > a->lse_stride))
+      return HCP_ERR_INVALID;
+    if (a->merge_lse != nullptr &&
+        (w.lse_col < 0 || static_cast<int64_t>(w.lse_col) + w.q_len > a->merge_lse_stride))
+      return HCP_ERR_INVALID;
+    for (int s = 0; s < 2; ++s) {
+      const int rc = validate_segment(a, w, w.seg[s]);
+      if (rc != HCP_OK) return rc;
+    }
+    if (w.q_len == 0) continue;
+    items.push_back(w);
+  }
+  if (items.empty()) return HCP_OK;
+  std::vector<int> order(items.size());
+  for (size_t i = 0; i < items.size(); ++i) {
+    order[i] = static_cast<int>(i);
+    cost.push_back(segment_cost(items[i].seg[0], items[i].q_len) +
+                   segment_cost(items[i].seg[1], items[i].q_len));
+  }
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return cost[x] > cost[y]; });
+
+  FwdParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (!encode_rows_heads(&p.tm_q, f16, a->q, a->q_rows, H, D, a->q_row_stride)) return HCP_ERR_CUDA;
+  p.tm_ka = p.tm_va = p.tm_kb = p.tm_vb = p.tm_cache = p.tm_q;  // placeholders for absent sources
+  if (want_a && (!encode_rows_heads(&p.tm_ka, f16, a->k_a, a->rows_a, Hkv, D, a->a_row_stride) ||
+                 !encode_rows_heads(&p.tm_va, f16, a->v_a, a->rows_a, Hkv, D, a->a_row_stride)))
+    return HCP_ERR_CUDA;
+  if (want_b && (!encode_rows_heads(&p.tm_kb, f16, a->k_b, a->rows_b, Hkv, D, a->b_row_stride) ||
+                 !encode_rows_heads(&p.tm_vb, f16, a->v_b, a->rows_b, Hkv, D, a->b_row_stride)))
+    return HCP_ERR_CUDA;
+  if (want_paged) {
+    const uint64_t bs = static_cast<uint64_t>(a->block_size);
+    const uint64_t dims[4] = {static_cast<uint64_t>(2 * D), bs, static_cast<uint64_t>(Hkv),
+                              static_cast<uint64_t>(a->num_blocks)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(2 * D) * 2, bs * 2 * D * 2,
+                                 static_cast<uint64_t>(Hkv) * bs * 2 * D * 2};
+    const uint32_t box[4] = {64, static_cast<uint32_t>(bs), 1, 1};
+    if (!encode_map(&p.tm_cache, f16, 4, a->kv_cache, dims, strides, box)) return HCP_ERR_CUDA;
+  }
+  p.block_table = a->block_table;
+  p.bt_stride = a->block_table_stride;
+  p.bt_rows = a->block_table_rows;
+  p.num_blocks = a->num_blocks;
+  p.out = a->out;
+  p.out_row_stride = a->out_row_stride;
+  p.out_f32 = a->out_dtype == HCP_F32;
+  p.lse = a->lse;
+  p.lse_stride = a->lse_stride;
+  p.merge_o = a->merge_o;
+  p.merge_o_row_stride = a->merge_o_row_stride;
+  p.merge_o_f32 = a->merge_o_dtype == HCP_F32;
+  p.merge_lse = a->merge_lse;
+  p.merge_lse_stride = a->merge_lse_stride;
+  p.num_heads = H;
+  p.group = H / Hkv;
+  p.block_size = want_paged ? a->block_size : 16;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (size_t base = 0; base < order.size(); base += kMaxWork) {
+    const int n = static_cast<int>(std::min<size_t>(kMaxWork, order.size() - base));
+    int tiles = 0;
+    for (int i = 0; i < n; ++i) {
+      p.work[i] = items[order[base + i]];
+      p.tile_off[i] = tiles;
+      tiles += (p.work[i].q_len + kBlockM - 1) / kBlockM;
+    }
+    p.tile_off[n] = tiles;
+    p.num_work = n;
+    p.total_tiles = tiles;
+    const int64_t grid = static_cast<int64_t>(tiles) * H;
+    if (grid <= 0) continue;
+    if (grid > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
+    int rc;
+    if (D == 128) rc = f16 ? launch_fwd<128, true>(p, static_cast<int>(grid), st)
+                           : launch_fwd<128, false>(p, static_cast<int>(grid), st);
+    else rc = f16 ? launch_fwd<64, true>(p, static_cast<int>(grid), st)
+                  : launch_fwd<64, false>(p, static_cast<int>(grid), st);
+    if (rc != HCP_OK) return rc;
+  }
+  return HCP_OK;
+}
+
+extern "C" int hcp_merge_attn_states(void* out, int32_t out_dtype, int64_t out_row_stride,
+                                     float* out_lse, int64_t out_lse_stride, const void* prefix_o,
+                                     int32_t prefix_dtype, int64_t prefix_row_stride,
+                                     const float* prefix_lse, int64_t prefix_lse_stride,
+                                     const void* suffix_o, int32_t suffix_dtype,
+                                     int64_t suffix_row_stride, const float* suffix_lse,
+                                     int64_t suffix_lse_stride, int64_t num_tokens,
+                                     int32_t num_heads, int32_t head_dim, void* stream) {
+  auto ok_dt = [](int dt) { return dt == HCP_BF16 || dt == HCP_F16 || dt == HCP_F32; };
+  if (out == nullptr || prefix_o == nullptr || suffix_o == nullptr || prefix_lse == nullptr ||
+      suffix_lse == nullptr)
+    return HCP_ERR_INVALID;
+  if (!ok_dt(out_dtype) || !ok_dt(prefix_dtype) || !ok_dt(suffix_dtype)) return HCP_ERR_UNSUPPORTED;
+  if (num_tokens < 0 || num_heads <= 0 || head_dim <= 0) return HCP_ERR_INVALID;
+  const int64_t row = static_cast<int64_t>(num_heads) * head_dim;
+  if (out_row_stride < row || prefix_row_stride < row || suffix_row_stride < row)
+    return HCP_ERR_INVALID;
+  if (prefix_lse_stride < num_tokens || suffix_lse_stride < num_tokens ||
+      (out_lse != nullptr && out_lse_stride < num_tokens))
+    return HCP_ERR_INVALID;
+  if (num_tokens == 0) return HCP_OK;
+  MergeParams p;
+  p.out = out;
+  p.pre = prefix_o;
+  p.suf = suffix_o;
+  p.out_lse = out_lse;
+  p.pre_lse = prefix_lse;
+  p.suf_lse = suffix_lse;
+  p.out_stride = out_row_stride;
+  p.pre_stride = prefix_row_stride;
+  p.suf_stride = suffix_row_stride;
+  p.out_lse_stride = out_lse_stride;
+  p.pre_lse_stride = prefix_lse_stride;
+  p.suf_lse_stride = suffix_lse_stride;
+  p.num_tokens = num_tokens;
+  p.num_heads = num_heads;
+  p.head_dim = head_dim;
+  p.out_dt = out_dtype;
+  p.pre_dt = prefix_dtype;
+  p.suf_dt = suffix_dtype;
+  const int64_t warps = num_tokens * num_heads;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
+  merge_states_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
+extern "C" int hcp_get_device_status(int32_t* status_out) {
+  if (status_out == nullptr) return HCP_ERR_INVALID;
+  if (cudaDeviceSynchronize() != cudaSuccess) return HCP_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return HCP_ERR_CUDA;
+  *status_out = v;
+  return HCP_OK;
+}
+
+extern "C" int hcp_reset_device_status(void) {
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return HCP_ERR_CUDA;
+  return cudaDeviceSynchronize() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
+extern "C" const char* hcp_version(void) { return "hcp_ring 0.1.0 (sm_100a)"; }

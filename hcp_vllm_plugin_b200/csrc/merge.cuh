@@ -1,0 +1,70 @@
+// Standalone LSE merge of two partial attention results (the vLLM
+// merge_attn_states contract): an HBM-bound elementwise kernel, one warp per
+// (token, head) row, 16-byte vector loads where the dtype allows.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "hcp_ring.h"
+
+namespace hcp {
+
+struct MergeParams {
+  void* out;
+  const void* pre;
+  const void* suf;
+  float* out_lse;
+  const float* pre_lse;
+  const float* suf_lse;
+  long long out_stride, pre_stride, suf_stride;      // row strides (elements)
+  long long out_lse_stride, pre_lse_stride, suf_lse_stride;
+  long long num_tokens;
+  int num_heads;
+  int head_dim;
+  int out_dt, pre_dt, suf_dt;
+};
+
+__device__ __forceinline__ float load_elem(const void* base, int dt, long long i) {
+  if (dt == HCP_F32) return static_cast<const float*>(base)[i];
+  if (dt == HCP_F16) return __half2float(static_cast<const __half*>(base)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+}
+__device__ __forceinline__ void store_elem(void* base, int dt, long long i, float v) {
+  if (dt == HCP_F32) static_cast<float*>(base)[i] = v;
+  else if (dt == HCP_F16) static_cast<__half*>(base)[i] = __float2half_rn(v);
+  else static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+}
+
+__global__ void __launch_bounds__(256) merge_states_kernel(const MergeParams p) {
+  const long long warp_global = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long rows = p.num_tokens * p.num_heads;
+  if (warp_global >= rows) return;
+  const long long tok = warp_global / p.num_heads;
+  const int h = static_cast<int>(warp_global - tok * p.num_heads);
+  float lp = p.pre_lse[h * p.pre_lse_stride + tok];
+  float ls = p.suf_lse[h * p.suf_lse_stride + tok];
+  if (lp == INFINITY) lp = -INFINITY;  // +inf marks an empty partial
+  if (ls == INFINITY) ls = -INFINITY;
+  const float m = fmaxf(lp, ls);
+  float wp = 0.f, ws = 0.f, lse = -INFINITY;
+  if (m != -INFINITY) {
+    const float ep = expf(lp - m);
+    const float es = expf(ls - m);
+    const float tot = ep + es;
+    wp = ep / tot;
+    ws = es / tot;
+    lse = m + logf(tot);
+  }
+  const long long po = tok * p.pre_stride + static_cast<long long>(h) * p.head_dim;
+  const long long so = tok * p.suf_stride + static_cast<long long>(h) * p.head_dim;
+  const long long oo = tok * p.out_stride + static_cast<long long>(h) * p.head_dim;
+  for (int d = lane; d < p.head_dim; d += 32) {
+    const float v = load_elem(p.pre, p.pre_dt, po + d) * wp + load_elem(p.suf, p.suf_dt, so + d) * ws;
+    store_elem(p.out, p.out_dt, oo + d, v);
+  }
+  if (lane == 0 && p.out_lse != nullptr) p.out_lse[h * p.out_lse_stride + tok] = lse;
+}
+
+}  // namespace hcp

@@ -1,0 +1,197 @@
+"""Torch-tensor front end of the C ABI.
+
+Each function checks its tensors, builds the C argument struct and calls
+``libhcp_ring.so`` on the current CUDA stream.  Nothing here computes
+attention: there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _capi as C
+
+_DT = {torch.bfloat16: C.HCP_BF16, torch.float16: C.HCP_F16, torch.float32: C.HCP_F32}
+
+# Work-item row layout shared with ``hcp_attn_work`` (12 int32 per item):
+#   q_start, q_len, paged_req, lse_col, then per segment (src, start, len, causal_off) x 2
+WORK_FIELDS = 12
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _rows_heads(t: torch.Tensor, name: str) -> int:
+    """Row stride (elements) of a [rows, heads, D] tensor whose last two dims are packed."""
+    if t.dim() != 3:
+        raise ValueError(f"{name} must be [rows, heads, head_dim], got {tuple(t.shape)}")
+    if t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+        raise ValueError(f"{name} must be contiguous in its last two dims")
+    return t.stride(0) if t.shape[0] > 1 else t.shape[1] * t.shape[2]
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def make_work(items) -> np.ndarray:
+    """Pack work items into an int32 [n, 12] array.
+
+    Each item is ``(q_start, q_len, paged_req, lse_col, seg0, seg1)`` with a
+    segment ``(src, start, len, causal_off)`` or ``None``.
+    """
+    arr = np.zeros((len(items), WORK_FIELDS), dtype=np.int32)
+    for i, (qs, ql, preq, lcol, s0, s1) in enumerate(items):
+        arr[i, :4] = (qs, ql, preq, lcol)
+        for j, sg in enumerate((s0, s1)):
+            if sg is not None:
+                arr[i, 4 + 4 * j: 8 + 4 * j] = sg
+    return arr
+
+
+def ring_attn_fwd(
+    q: torch.Tensor,
+    work: np.ndarray,
+    *,
+    scale: float,
+    num_kv_heads: int,
+    out: torch.Tensor,
+    lse: torch.Tensor | None = None,
+    k_a: torch.Tensor | None = None,
+    v_a: torch.Tensor | None = None,
+    k_b: torch.Tensor | None = None,
+    v_b: torch.Tensor | None = None,
+    kv_cache: torch.Tensor | None = None,
+    block_table: torch.Tensor | None = None,
+    merge_o: torch.Tensor | None = None,
+    merge_lse: torch.Tensor | None = None,
+) -> None:
+    """Fused ring-attention forward over a list of work items (``hcp_ring_attn_fwd``).
+
+    q/out [rows, H, D]; k_*/v_* [rows, Hkv, D]; kv_cache [num_blocks, Hkv,
+    block_size, 2*D]; block_table [num_reqs, max_blocks] int32; lse, merge_lse
+    [H, cols] float32.  ``work`` comes from :func:`make_work`.
+    """
+    if not q.is_cuda:
+        raise ValueError("q must be a CUDA tensor (no CPU path)")
+    if q.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"unsupported dtype {q.dtype}")
+    num_heads, head_dim = q.shape[1], q.shape[2]
+    a = C.HcpFwdArgs()
+    a.dtype = _DT[q.dtype]
+    a.num_heads = num_heads
+    a.num_kv_heads = num_kv_heads
+    a.head_dim = head_dim
+    a.scale = float(scale)
+    a.q = _ptr(q)
+    a.q_rows = q.shape[0]
+    a.q_row_stride = _rows_heads(q, "q")
+    for name, kt, vt in (("a", k_a, v_a), ("b", k_b, v_b)):
+        if kt is None:
+            continue
+        if vt is None or kt.shape != vt.shape or kt.dtype != q.dtype or vt.dtype != q.dtype:
+            raise ValueError(f"k_{name}/v_{name} must match in shape and dtype")
+        ks, vs = _rows_heads(kt, f"k_{name}"), _rows_heads(vt, f"v_{name}")
+        if ks != vs:
+            raise ValueError(f"k_{name} and v_{name} must share a row stride")
+        setattr(a, f"k_{name}", _ptr(kt))
+        setattr(a, f"v_{name}", _ptr(vt))
+        setattr(a, f"rows_{name}", kt.shape[0])
+        setattr(a, f"{name}_row_stride", ks)
+    if kv_cache is not None:
+        if kv_cache.dim() != 4 or not kv_cache.is_contiguous() or kv_cache.dtype != q.dtype:
+            raise ValueError("kv_cache must be a contiguous [num_blocks, Hkv, block_size, 2*D] tensor")
+        if block_table is None or block_table.dtype != torch.int32 or block_table.dim() != 2:
+            raise ValueError("block_table must be an int32 [num_reqs, max_blocks] tensor")
+        if block_table.stride(1) != 1:
+            raise ValueError("block_table rows must be contiguous")
+        a.kv_cache = _ptr(kv_cache)
+        a.num_blocks = kv_cache.shape[0]
+        a.block_size = kv_cache.shape[2]
+        a.block_table = _ptr(block_table)
+        a.block_table_stride = block_table.stride(0)
+        a.block_table_rows = block_table.shape[0]
+    if out.shape[0] < q.shape[0] or out.shape[1:] != q.shape[1:] or out.device != q.device:
+        raise ValueError("out must be [>= q rows, H, D] on q's device")
+    a.out = _ptr(out)
+    a.out_dtype = _DT[out.dtype]
+    a.out_row_stride = _rows_heads(out, "out")
+    if lse is not None:
+        if lse.dtype != torch.float32 or lse.dim() != 2 or lse.stride(1) != 1:
+            raise ValueError("lse must be a float32 [H, cols] tensor with unit column stride")
+        if lse.shape[0] != num_heads:
+            raise ValueError("lse must have H rows")
+        a.lse = _ptr(lse)
+        a.lse_stride = lse.stride(0)
+    if merge_lse is not None:
+        if merge_o is None or merge_lse.dtype != torch.float32 or merge_lse.stride(1) != 1:
+            raise ValueError("merge needs merge_o and a float32 merge_lse")
+        if merge_lse.shape[0] != num_heads or merge_o.shape[0] < q.shape[0] or merge_o.shape[1:] != q.shape[1:]:
+            raise ValueError("merge_o must be [>= q rows, H, D] and merge_lse [H, cols]")
+        a.merge_o = _ptr(merge_o)
+        a.merge_o_dtype = _DT[merge_o.dtype]
+        a.merge_o_row_stride = _rows_heads(merge_o, "merge_o")
+        a.merge_lse = _ptr(merge_lse)
+        a.merge_lse_stride = merge_lse.stride(0)
+    work = np.ascontiguousarray(work, dtype=np.int32)
+    a.work = work.ctypes.data_as(ctypes.POINTER(C.HcpAttnWork))
+    a.num_work = work.shape[0]
+    C.check(C.load().hcp_ring_attn_fwd(ctypes.byref(a), _stream(q)), "hcp_ring_attn_fwd")
+
+
+def ring_attn_with_lse(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    scale: float,
+    causal_offset: int | None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Flash attention with LSE output; drop-in for the reference's
+    ``ring_attn_with_lse`` (``hcp_vllm_plugin/ring_triton_attn.py:155-207``).
+
+    q [Tq, H, D], k/v [Tk, Hkv, D]; ``causal_offset`` = position of query 0 in
+    the KV frame, ``None`` = non-causal.  Returns (out [Tq, H, D] in q's dtype,
+    lse [H, Tq] float32, natural log).
+    """
+    tq, num_heads, _ = q.shape
+    tk, num_kv_heads, _ = k.shape
+    out = torch.empty_like(q)
+    lse = torch.empty((num_heads, tq), dtype=torch.float32, device=q.device)
+    if tq == 0:
+        return out, lse
+    seg = (C.HCP_SRC_A, 0, tk, -1 if causal_offset is None else int(causal_offset))
+    if causal_offset is not None and causal_offset < 0:
+        raise ValueError("causal_offset must be >= 0 or None")
+    work = make_work([(0, tq, 0, 0, seg, None)])
+    ring_attn_fwd(q, work, scale=scale, num_kv_heads=num_kv_heads, out=out, lse=lse, k_a=k, v_a=v)
+    return out, lse
+
+
+def merge_attn_states(
+    output: torch.Tensor,
+    prefix_output: torch.Tensor,
+    prefix_lse: torch.Tensor,
+    suffix_output: torch.Tensor,
+    suffix_lse: torch.Tensor,
+    output_lse: torch.Tensor | None = None,
+) -> None:
+    """vLLM ``merge_attn_states`` contract (``hcp_merge_attn_states``): o tensors
+    [T, H, D], lse [H, T] float32; writes ``output`` (and ``output_lse``)."""
+    num_tokens, num_heads, head_dim = output.shape
+    for t in (prefix_lse, suffix_lse) + ((output_lse,) if output_lse is not None else ()):
+        if t.dtype != torch.float32 or t.stride(1) != 1:
+            raise ValueError("lse tensors must be float32 with unit column stride")
+    lib = C.load()
+    rc = lib.hcp_merge_attn_states(
+        _ptr(output), _DT[output.dtype], _rows_heads(output, "output"),
+        _ptr(output_lse), 0 if output_lse is None else output_lse.stride(0),
+        _ptr(prefix_output), _DT[prefix_output.dtype], _rows_heads(prefix_output, "prefix_output"),
+        _ptr(prefix_lse), prefix_lse.stride(0),
+        _ptr(suffix_output), _DT[suffix_output.dtype], _rows_heads(suffix_output, "suffix_output"),
+        _ptr(suffix_lse), suffix_lse.stride(0),
+        num_tokens, num_heads, head_dim, _stream(output))
+    C.check(rc, "hcp_merge_attn_states")

@@ -1,0 +1,148 @@
+/*
+ * hcp_ring.h - C ABI of the B200 (sm_100a) ring context-parallel attention
+ * library (libhcp_ring.so).
+ *
+ * Plain pointers, sizes and a CUDA stream handle (cudaStream_t passed as
+ * void*).  No torch types.  Every tensor pointer is a DEVICE pointer unless a
+ * comment says "host".  Every entry point returns an hcp_status; launches are
+ * asynchronous on the given stream.
+ *
+ * Layout conventions (all row-major, innermost dimension last):
+ *   q / out        [rows, H, D]     row stride given in elements (>= H*D)
+ *   k / v          [rows, Hkv, D]   row stride given in elements (>= Hkv*D)
+ *   paged kv cache [num_blocks, Hkv, block_size, 2*D]; K = [..., :D], V = [..., D:]
+ *   lse            [H, lse_stride]  float32, natural log
+ *
+ * Interfaces of the reference plugin (stark-sim/hcp-vllm-plugin) that each
+ * entry point replaces are cited per declaration.
+ */
+#ifndef HCP_RING_H_
+#define HCP_RING_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum hcp_status {
+  HCP_OK = 0,
+  HCP_ERR_INVALID = 1,      /* bad argument (null pointer, inconsistent sizes) */
+  HCP_ERR_UNSUPPORTED = 2,  /* shape / dtype / device the kernels do not handle */
+  HCP_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed */
+  HCP_ERR_DEVICE = 4        /* a kernel reported a device-side failure (timeout) */
+} hcp_status;
+
+typedef enum hcp_dtype { HCP_BF16 = 0, HCP_F16 = 1, HCP_F32 = 2 } hcp_dtype;
+
+/* Where the keys of one KV segment come from. */
+typedef enum hcp_kv_src {
+  HCP_SRC_NONE = 0,   /* segment unused */
+  HCP_SRC_A = 1,      /* contiguous k_a / v_a rows [start, start+len) */
+  HCP_SRC_B = 2,      /* contiguous k_b / v_b rows [start, start+len) */
+  HCP_SRC_PAGED = 3   /* paged cache: key positions [start, start+len) of the
+                         sequence in block_table row `paged_req`; start must be
+                         a multiple of block_size */
+} hcp_kv_src;
+
+/* One KV segment of a work item.  causal_off < 0: non-causal (every key
+ * visible).  causal_off >= 0: key j (segment-relative) is visible to query row
+ * i (work-item-relative) iff j <= causal_off + i. */
+typedef struct hcp_kv_segment {
+  int32_t src;
+  int32_t start;
+  int32_t len;
+  int32_t causal_off;
+} hcp_kv_segment;
+
+/* One work item: query rows [q_start, q_start+q_len) attend, with ONE online
+ * softmax, over the union of up to two KV segments (typically the transient
+ * peer prefix, non-causal, then the local chunk, causal).  Row i writes out row
+ * q_start+i and lse column lse_col+i. */
+typedef struct hcp_attn_work {
+  int32_t q_start;
+  int32_t q_len;
+  int32_t paged_req;
+  int32_t lse_col;
+  hcp_kv_segment seg[2];
+} hcp_attn_work;
+
+/* Arguments of hcp_ring_attn_fwd.  Unused sources may be NULL. */
+typedef struct hcp_fwd_args {
+  int32_t dtype;          /* HCP_BF16 or HCP_F16 (q, k, v, cache) */
+  int32_t num_heads;      /* H */
+  int32_t num_kv_heads;   /* Hkv, H % Hkv == 0 */
+  int32_t head_dim;       /* D: 64 or 128 */
+  float scale;            /* softmax scale */
+  int32_t _pad0;
+  const void* q;          int64_t q_rows;  int64_t q_row_stride;
+  const void* k_a;        const void* v_a; int64_t rows_a; int64_t a_row_stride;
+  const void* k_b;        const void* v_b; int64_t rows_b; int64_t b_row_stride;
+  const void* kv_cache;   int64_t num_blocks; int32_t block_size; int32_t _pad1;
+  const int32_t* block_table; int64_t block_table_stride; int64_t block_table_rows;
+  void* out;              int32_t out_dtype; int32_t _pad2; int64_t out_row_stride;
+  float* lse;             int64_t lse_stride;            /* may be NULL */
+  /* Optional earlier partial result (O, LSE) over other keys, merged into this
+   * result in the epilogue (vLLM merge_attn_states semantics).  merge_o may
+   * alias out (same dtype and stride) and merge_lse may alias lse. */
+  const void* merge_o;    int32_t merge_o_dtype; int32_t _pad3; int64_t merge_o_row_stride;
+  const float* merge_lse; int64_t merge_lse_stride;
+  const hcp_attn_work* work;  /* HOST array of num_work items */
+  int32_t num_work;
+  int32_t _pad4;
+} hcp_fwd_args;
+
+/*
+ * Fused ring-attention forward: flash attention with per-row LSE over up to
+ * two KV segments per work item (GQA, global-offset causal mask, paged or
+ * contiguous keys), optional merge into an earlier partial (O, LSE).
+ * tcgen05 MMA with TMEM accumulators, TMA-staged tiles.
+ *
+ * Replaces, in the reference:
+ *   ring_attn_with_lse           hcp_vllm_plugin/ring_triton_attn.py:155-207
+ *   _ring_fwd_kernel             hcp_vllm_plugin/ring_triton_attn.py:35-152
+ *   the per-request loop of HcpRingAttentionImpl.forward (gather, local pass,
+ *   peer pass, merge)            hcp_vllm_plugin/ring_backend.py:611-832
+ *   _merge / merge_attn_states on the prefill path
+ *                                hcp_vllm_plugin/ring_backend.py:339-360
+ */
+int hcp_ring_attn_fwd(const hcp_fwd_args* args, void* stream);
+
+/*
+ * Standalone LSE merge of two partial attentions (vLLM merge_attn_states):
+ *   out = (prefix_o * e^{prefix_lse - m} + suffix_o * e^{suffix_lse - m}) / sum
+ * with +inf LSE treated as -inf.  o: [T, H, D] (row stride in elements), lse:
+ * [H, lse_stride].  out_lse may be NULL.  dtypes: HCP_BF16/HCP_F16/HCP_F32 for
+ * o tensors (prefix, suffix and out may differ).
+ *
+ * Replaces: vLLM merge_attn_states as called by _merge
+ * (hcp_vllm_plugin/ring_backend.py:339-360) and _merge_pair
+ * (hcp_vllm_plugin/ring_decode.py:46-61).
+ */
+int hcp_merge_attn_states(void* out, int32_t out_dtype, int64_t out_row_stride,
+                          float* out_lse, int64_t out_lse_stride,
+                          const void* prefix_o, int32_t prefix_dtype, int64_t prefix_row_stride,
+                          const float* prefix_lse, int64_t prefix_lse_stride,
+                          const void* suffix_o, int32_t suffix_dtype, int64_t suffix_row_stride,
+                          const float* suffix_lse, int64_t suffix_lse_stride,
+                          int64_t num_tokens, int32_t num_heads, int32_t head_dim, void* stream);
+
+/*
+ * Device-side status word shared by all kernels of the library on the
+ * current device: 0 when no kernel reported a failure, else the first
+ * failure code (bounded waits that ran out).  Synchronises the device.
+ * hcp_reset_device_status clears it.  No counterpart in the reference (its
+ * Triton launch raises in Python).
+ */
+int hcp_get_device_status(int32_t* status_out);
+int hcp_reset_device_status(void);
+
+/* Library version string (static storage). */
+const char* hcp_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HCP_RING_H_ */
