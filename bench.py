@@ -1,0 +1,398 @@
+"""Ring context-parallel prefill benchmark.
+
+One step = the attention of all 28 layers of a 131072-token sequence split
+into N contiguous chunks, one per GPU (Qwen2.5-7B attention geometry: 28
+query heads, 4 KV heads, head_dim 128, bf16, seeded N(0,1) synthetic q/k/v,
+one set per layer).  Each rank durably holds only its own chunk; peer K/V
+rotate over NVLink every layer (``hcp_vllm_plugin_b200.ring_runner``).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Prints one JSON line on rank 0.  ``value`` is whole-job tokens/s measured on
+the device (CUDA events, barrier + synchronize around the timed steps, max
+over ranks).  ``e2e`` repeats the measurement through the public API with
+every layer's q/k/v copied from pinned host memory and the output copied
+back.  ``--impl reference`` times the reference algorithm's CPU path (the
+oracle port of its fp32 torch path) on a bounded sample and extrapolates.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ring-attn TFLOP/s (% bf16 peak); 128k ring-prefill tok/s at 1/2/4/8 B200"
+H, HKV, D = 28, 4, 128
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def causal_pairs(n: int) -> int:
+    return n * (n + 1) // 2
+
+
+def step_flops(seq: int, layers: int) -> float:
+    return 4.0 * D * H * causal_pairs(seq) * layers
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the ring-attention kernel from the committed
+    ncu summary (profiles/ring_fwd_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "ring_fwd_traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"hcp_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(seq: int, rows: int, seed: int = 0):
+    """Time the oracle (the reference's fp32 torch algorithm restated in numpy)
+    on the last ``rows`` query rows of one layer (each sees ~``seq`` keys).
+    Returns (seconds, flops of the sample, threads)."""
+    import numpy as np
+
+    from oracle import ring_oracle as ro
+
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((rows, H, D), dtype=np.float32)
+    k = rng.standard_normal((seq, HKV, D), dtype=np.float32)
+    v = rng.standard_normal((seq, HKV, D), dtype=np.float32)
+    q, k, v = ro.round_bf16(q), ro.round_bf16(k), ro.round_bf16(v)
+    t0 = time.perf_counter()
+    ro.attn_with_lse(q, k, v, D ** -0.5, seq - rows, q_block=rows)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * D * H * ro.visible_pairs(rows, seq, seq - rows)
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([x.get("num_threads", 1) for x in threadpool_info()] or [1])
+    except Exception:  # noqa: BLE001
+        threads = os.cpu_count() or 1
+    return dt, flops, threads
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    seq, layers = args.seq, args.layers
+    rows = args.cpu_rows
+    total = step_flops(seq, layers)
+    for _ in range(args.warmup):
+        cpu_sample(seq, rows)
+    rates = []
+    threads = 1
+    for _ in range(args.steps):
+        dt, fl, threads = cpu_sample(seq, rows)
+        rates.append(fl / dt)
+    rate = statistics.median(rates)
+    tok_s = seq / (total / rate)
+    sample = (f"one layer, last {rows} query rows x {seq} keys causal, 28 heads, fp32 numpy "
+              f"(oracle port of ring_backend.py:366-406), extrapolated by FLOPs to {layers} layers")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / rate, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config(args), "tflops": rate / 1e12,
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config(args):
+    return {"workload": "cfg3 ring CP prefill, attention only", "seq_len": args.seq,
+            "layers": args.layers, "heads": H, "kv_heads": HKV, "head_dim": D,
+            "chunk_per_gpu": args.seq // max(1, args.gpus), "parallelism": f"cp{args.gpus}",
+            "global_batch": 1, "l2": "inputs larger than L2 (q 0.94 GB/layer at N=1)",
+            "schedule": "balanced pairs" if not args.no_balance else "plain ring"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seq", type=int, default=131072)
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--cpu-rows", type=int, default=32)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-balance", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        args.gpus = world
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from hcp_vllm_plugin_b200 import _capi
+    from hcp_vllm_plugin_b200.ring_runner import RingPrefill
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    _capi.load()
+    seq, L = args.seq, args.layers
+    chunk = seq // world
+    scale = D ** -0.5
+    runner = RingPrefill(seq, H, HKV, D, scale, dev, balance=not args.no_balance)
+
+    # resident per-layer inputs of this rank's chunk (seeded)
+    qs, ks, vs = [], [], []
+    for layer in range(L):
+        g = torch.Generator(device=dev).manual_seed(1000 * layer + 17)
+        # generate the full layer's rows deterministically, keep this rank's chunk
+        q = torch.empty(chunk, H, D, dtype=torch.bfloat16, device=dev)
+        k = torch.empty(chunk, HKV, D, dtype=torch.bfloat16, device=dev)
+        v = torch.empty(chunk, HKV, D, dtype=torch.bfloat16, device=dev)
+        g.manual_seed(1000 * layer + 17 + 7919 * rank)
+        q.normal_(generator=g)
+        k.normal_(generator=g)
+        v.normal_(generator=g)
+        qs.append(q)
+        ks.append(k)
+        vs.append(v)
+    out = torch.empty(chunk, H, D, dtype=torch.bfloat16, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        for layer in range(L):
+            runner.forward(qs[layer], ks[layer], vs[layer], out)
+    _capi.check(0, "warmup")
+    barrier()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    stream = torch.cuda.current_stream(dev)
+    ev_layer = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(args.steps * L)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    launches0 = runner.launches
+    barrier()
+    t_start.record(stream)
+    i = 0
+    for _ in range(args.steps):
+        for layer in range(L):
+            ev_layer[i][0].record(stream)
+            runner.forward(qs[layer], ks[layer], vs[layer], out)
+            ev_layer[i][1].record(stream)
+            i += 1
+    t_end.record(stream)
+    barrier()
+    clk = clocks.stop()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    launches = runner.launches - launches0
+    layer_ms = [a.elapsed_time(b) for a, b in ev_layer]
+    status = _capi.device_status()
+    if status != 0:
+        raise SystemExit(f"device reported failure {status:#x}")
+
+    value = seq * args.steps / (elapsed_ms / 1e3)
+    total_flops = step_flops(seq, L) * args.steps
+    tflops = total_flops / (elapsed_ms / 1e3) / 1e12
+    pk, pk_kind = peaks()
+    peak_tf = pk["bf16_tflops_sustained"]
+    # roofline of the dominant kernel: at N=1 each layer is exactly one launch
+    # of the ring-attention kernel; its algorithmic FLOPs are the causal pairs.
+    mean_layer_ms = statistics.mean(layer_ms)
+    my_flops_layer = step_flops(seq, 1) if world == 1 else (
+        4.0 * D * H * runner.chunk * runner.chunk * runner.plan.work_units(rank))
+    achieved = my_flops_layer / (mean_layer_ms / 1e3) / 1e12
+    traffic = profile_traffic()
+    roof = {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+            "frac": achieved / peak_tf,
+            "peak_source": f"bf16_tflops_sustained ({pk_kind})",
+            "traffic": None if traffic is None else traffic.get("bytes_per_launch_cfg3_n1"),
+            "kernel": "ring_fwd_kernel<128,bf16>",
+            "per_launch_ms": mean_layer_ms if world == 1 else None}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, runner, dev, chunk, L, barrier, max_over_ranks, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        dt, fl, threads = cpu_sample(seq, args.cpu_rows)
+        rate = fl / dt
+        cpu = {"value": seq / (step_flops(seq, L) / rate), "unit": "tok/s", "cores": threads,
+               "kind": "port",
+               "sample": f"one layer, last {args.cpu_rows} query rows x {seq} keys causal, fp32 "
+                         f"numpy oracle, {dt:.2f} s, extrapolated by FLOPs to {L} layers"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) q/k/v per layer)", "config": config(args),
+            "tflops": tflops, "pct_bf16_peak": 100.0 * tflops / peak_tf,
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def run_e2e(args, runner, dev, chunk, L, barrier, max_over_ranks, world):
+    """Same metric through RingPrefill.forward with inputs copied from pinned
+    host memory every layer and the output copied back; copies overlap compute
+    on separate streams (double-buffered device inputs)."""
+    import torch
+
+    nbuf = 2  # distinct host layers (alternating)
+    hq = [torch.randn(chunk, H, D).bfloat16().pin_memory() for _ in range(nbuf)]
+    hk = [torch.randn(chunk, HKV, D).bfloat16().pin_memory() for _ in range(nbuf)]
+    hv = [torch.randn(chunk, HKV, D).bfloat16().pin_memory() for _ in range(nbuf)]
+    hout = [torch.empty(chunk, H, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    dq = [torch.empty(chunk, H, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    dk = [torch.empty(chunk, HKV, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    dv = [torch.empty(chunk, HKV, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    dout = [torch.empty(chunk, H, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    h2d = torch.cuda.Stream(dev)
+    d2h = torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_free = [torch.cuda.Event() for _ in range(2)]
+    for e in in_free + out_free:
+        e.record(comp)
+
+    def one_step():
+        for layer in range(L):
+            b = layer % 2
+            hb = layer % nbuf
+            with torch.cuda.stream(h2d):
+                h2d.wait_event(in_free[b])
+                dq[b].copy_(hq[hb], non_blocking=True)
+                dk[b].copy_(hk[hb], non_blocking=True)
+                dv[b].copy_(hv[hb], non_blocking=True)
+                in_ready[b].record(h2d)
+            comp.wait_event(in_ready[b])
+            comp.wait_event(out_free[b])
+            runner.forward(dq[b], dk[b], dv[b], dout[b])
+            in_free[b].record(comp)
+            out_ready[b].record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(out_ready[b])
+                hout[b].copy_(dout[b], non_blocking=True)
+                out_free[b].record(d2h)
+
+    one_step()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t0.record(comp)
+    for _ in range(args.steps):
+        one_step()
+    comp.wait_stream(d2h)
+    t1.record(comp)
+    barrier()
+    ms = max_over_ranks(t0.elapsed_time(t1))
+    bi = L * (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2 * world
+    bo = L * hout[0].numel() * 2 * world
+    return {"value": args.seq * args.steps / (ms / 1e3), "unit": "tok/s",
+            "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+            "note": "RingPrefill.forward per layer, q/k/v H2D from pinned host and output D2H "
+                    "every layer inside the timed region (2 distinct host layers alternate)"}
+
+
+if __name__ == "__main__":
+    main()

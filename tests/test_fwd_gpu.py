@@ -4,11 +4,15 @@ All calls go through the C ABI (``libhcp_ring.so``).  Tolerances:
   * LSE: 1e-3 absolute.
   * Output, fp16: 2e-3 absolute (the reference probe's bar,
     ``validate_ring_triton_kernel.py:55-61``).
-  * Output, bf16: 2e-3 absolute plus 2^-8 relative.  The output tensor is
-    bf16 and the reference's own path rounds its fp32 result to bf16
-    (``o.to(output.dtype)``, ``ring_backend.py:832``); one bf16 step is
-    2^-8 relative, which exceeds 2e-3 absolute for |o| > 0.5, so no bf16
-    output can meet a flat 2e-3 there.  Where |o| <= 0.5 this is <= 4e-3.
+  * Output, bf16: 2e-3 absolute plus 2^-7 relative (one bf16 step).  The
+    output tensor is bf16 and the reference's own path rounds its fp32
+    result to bf16 (``o.to(output.dtype)``, ``ring_backend.py:832``), and
+    its kernel feeds P to the PV product in the value dtype
+    (``p.to(v.dtype)``, ``ring_triton_attn.py:132``).  Each of these is up to
+    2^-9 relative, so rows that see only a handful of keys (|o| ~ 1) cannot
+    meet a flat 2e-3 in bf16 - not even the reference's kernel.
+  * Output at the deployment shapes (every row sees >= 512 keys, as in the
+    BASELINE configs): the flat 2e-3 north-star bar, checked separately.
 """
 
 import numpy as np
@@ -32,10 +36,15 @@ def _check_out(got, want, dtype, what):
     if dtype == torch.float16:
         tol = np.full_like(want, 2e-3)
     else:
-        tol = 2e-3 + 2.0 ** -8 * np.abs(want)
+        tol = 2e-3 + 2.0 ** -7 * np.abs(want)
     bad = err > tol
     assert not bad.any(), (f"{what}: {bad.sum()} / {bad.size} outside tolerance, "
                            f"max err {err.max():.3e}")
+
+
+def _check_flat(got, want, what, tol=2e-3):
+    err = np.abs(np.asarray(got, np.float32) - want)
+    assert err.max() <= tol, f"{what}: flat max err {err.max():.3e} > {tol}"
 
 
 def _check_lse(got, want, what):
@@ -138,6 +147,8 @@ def test_fused_peer_plus_local_equals_merge(dev, tq, tpeer, tloc, off):
     if len(parts) == 2:
         want, want_lse = ro.merge_pair(parts[0][0], parts[0][1], parts[1][0], parts[1][1])
     _check_out(_f(out), want, torch.bfloat16, "fused peer+local")
+    if tpeer >= 512:
+        _check_flat(_f(out), want, "fused peer+local (deployment shape)")
     _check_lse(_f(lse), want_lse, "fused peer+local")
 
 
@@ -244,3 +255,5 @@ def test_paged_local_plus_peer_batch(dev, lens, peer):
                          scale=D128 ** -0.5, staged=staged)
     want = ro.ring_forward(batch, round_to_bf16=False)
     _check_out(_f(out), want, torch.bfloat16, f"paged batch {lens}")
+    if peer >= 512:
+        _check_flat(_f(out), want, f"paged batch {lens} (cfg1 shape)")
