@@ -7,27 +7,34 @@
 // partial (O, LSE) can be merged in the epilogue, so ring hops chain without a
 // separate merge kernel.
 //
-// Warp roles (192 threads):
-//   warps 0-3  softmax / O correction / epilogue; thread t owns query row t,
-//              which is TMEM lane t
-//   warp 4     TMA producer: Q once, then K and V tiles through a 2-stage ring
+// Warp roles (320 threads):
+//   warps 0-7  softmax / O correction / epilogue.  Query row r of the tile is
+//              TMEM lane r; warp w handles lanes 32*(w%4).. and key/column half
+//              w/4 of every S tile (two threads per row, which keeps two
+//              softmax warps per SM sub-partition in flight).  The two halves
+//              of a row exchange their partial row max through shared memory
+//              once per KV tile (bounded mbarrier, never bar.sync).
+//   warp 8     TMA producer: Q once, then K and V tiles through a 2-stage ring
 //              (contiguous 3-D tensor maps, or 4-D maps over the paged cache
 //              indexed through the block table)
-//   warp 5     tcgen05 MMA issuer (one elected lane) and TMEM owner
+//   warp 9     tcgen05 MMA issuer (one lane) and TMEM owner
 //
 // TMEM (512 columns x 128 lanes, fp32):
-//   [  0,128)  S buffer 0      S = Q K^T for even KV tiles; P (16-bit, two keys
-//   [128,256)  S buffer 1      per column) is written back over its first 64
-//                              columns and feeds O += P V as the A operand
+//   [  0,128)  S buffer 0      S = Q K^T of even KV tiles.  P (16-bit, two keys
+//   [128,256)  S buffer 1      per column) is written back over columns 0-63 and
+//                              feeds O += P V as the A operand; for short rows
+//                              the low part P - bf16(P) goes to columns 64-127
+//                              and is accumulated by a second PV product
 //   [256,256+D) O accumulator
 //
 // Shared memory (1024-byte aligned, 128-byte swizzle, 64-element boxes):
-//   Q tile, then per stage a K tile and a V tile, then the mbarriers.
+//   Q tile, then per stage a K tile and a V tile, then the row-max exchange
+//   buffers and the mbarriers.
 //
 // Numerics: scores are scaled into the base-2 domain (scale * log2 e), the
 // running max is only raised when a tile's max exceeds it by more than 8
-// (P stays <= 2^8, exact in bf16/fp16 range), and O is rescaled in TMEM only
-// then.  LSE = (m + log2 l) * ln 2.
+// (P stays <= 2^8) and O is rescaled in TMEM only then.
+// LSE = (m + log2 l) * ln 2.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -43,13 +50,16 @@ __device__ int g_device_status = 0;
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
-constexpr int kWarpTma = 4;
-constexpr int kWarpMma = 5;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kWarpTma = 8;
+constexpr int kWarpMma = 9;
+constexpr int kThreads = 320;
 constexpr int kMaxWork = 160;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
 constexpr float kRescaleThreshold = 8.0f;            // log2 units
+constexpr int kPreciseKeys = 256;  // rows seeing fewer keys get the hi+lo P product
 
 // Failure codes written to g_device_status.
 enum : int {
@@ -91,7 +101,7 @@ struct FwdParams {
 };
 
 // Bounded mbarrier wait.  Returns false when this CTA aborted (this wait ran
-// out of time, or another role of the CTA already gave up).
+// out of time, another role of the CTA gave up, or another CTA failed).
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                          int code) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -101,7 +111,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
     if ((it & 63u) == 0) {
       if (*abort_flag) return false;
       if (*reinterpret_cast<volatile int*>(&g_device_status) != 0) {
-        *abort_flag = 1;  // another CTA already failed: give up quickly
+        *abort_flag = 1;
         return false;
       }
       if (ptx::global_timer_ns() - t0 > kWaitTimeoutNs) {
@@ -158,7 +168,7 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
   }
 }
 
-// Tiles of segment s for a query tile whose valid rows are [q0, q0+rows).
+// Keys of segment `sg` visible to the valid rows [q0, q0+rows) of a query tile.
 __device__ __forceinline__ int segment_keys(const hcp_kv_segment& sg, int q0, int rows) {
   if (sg.src == HCP_SRC_NONE || sg.len <= 0) return 0;
   if (sg.causal_off < 0) return sg.len;
@@ -166,13 +176,24 @@ __device__ __forceinline__ int segment_keys(const hcp_kv_segment& sg, int q0, in
   return static_cast<int>(max(0ll, min(static_cast<long long>(sg.len), last_visible)));
 }
 
+template <int D>
+struct FwdSmem {
+  static constexpr int kBoxBytes = 128 * 128;  // 128 rows x 64 elems x 2 B
+  static constexpr int kTileBytes = (D / 64) * kBoxBytes;
+  static constexpr int kNumBars = 9 + 4 * kStages;
+  static constexpr int kRedOff = kTileBytes * (1 + 2 * kStages);  // float red[2][2][128]
+  static constexpr int kBarOff = kRedOff + 2 * 2 * 128 * 4;
+  static constexpr int kEnd = kBarOff + 8 * kNumBars + 16;
+  static constexpr int kBytes = kEnd + 1024;  // + alignment slack
+};
+
 template <int D, bool F16>
 __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_constant__ FwdParams p) {
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
+  using L = FwdSmem<D>;
   constexpr int kHalves = D / 64;
-  constexpr int kBoxBytes = 128 * 128;          // 128 rows x 64 elems x 2 B
-  constexpr int kTileBytes = kHalves * kBoxBytes;
-  constexpr int kNumBars = 7 + 4 * kStages;
+  constexpr int kBoxBytes = L::kBoxBytes;
+  constexpr int kTileBytes = L::kTileBytes;
   constexpr uint32_t kIdescQK = ptx::idesc_f16(128, 128, false, false, F16);
   constexpr uint32_t kIdescPV = ptx::idesc_f16(128, D, false, true, F16);
 
@@ -181,11 +202,11 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t s_q = ptx::smem_u32(smem);
   const uint32_t s_kv0 = s_q + kTileBytes;  // stage s: K at +2s tiles, V at +2s+1 tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTileBytes * (1 + 2 * kStages));
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  float* red = reinterpret_cast<float*>(smem + L::kRedOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const uint32_t bar0 = ptx::smem_u32(bars);
-  // barrier addresses
   const uint32_t b_q = bar0;
   auto b_kfull = [&](int s) { return bar0 + 8u * (1 + s); };
   auto b_kempty = [&](int s) { return bar0 + 8u * (1 + kStages + s); };
@@ -193,8 +214,9 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   auto b_vempty = [&](int s) { return bar0 + 8u * (1 + 3 * kStages + s); };
   auto b_sfull = [&](int b) { return bar0 + 8u * (1 + 4 * kStages + b); };
   auto b_pfull = [&](int b) { return bar0 + 8u * (3 + 4 * kStages + b); };
-  const uint32_t b_odone = bar0 + 8u * (5 + 4 * kStages);
-  const uint32_t b_final = bar0 + 8u * (6 + 4 * kStages);
+  auto b_red = [&](int b) { return bar0 + 8u * (5 + 4 * kStages + b); };
+  const uint32_t b_odone = bar0 + 8u * (7 + 4 * kStages);
+  const uint32_t b_final = bar0 + 8u * (8 + 4 * kStages);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -218,6 +240,9 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   const int keys1 = segment_keys(wk.seg[1], q0, rows_valid);
   const int tiles0 = (keys0 + kBlockN - 1) / kBlockN;
   const int n_tiles = tiles0 + (keys1 + kBlockN - 1) / kBlockN;
+  // Rows that see few keys in total get P as hi + lo 16-bit parts.
+  const bool precise =
+      segment_keys(wk.seg[0], q0, 1) + segment_keys(wk.seg[1], q0, 1) < kPreciseKeys;
 
   // ---- setup
   if (threadIdx.x == 0) {
@@ -230,7 +255,8 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(b_sfull(b), 1);
-      ptx::mbar_init(b_pfull(b), 128);
+      ptx::mbar_init(b_pfull(b), kSoftmaxThreads);
+      ptx::mbar_init(b_red(b), kSoftmaxWarps);
     }
     ptx::mbar_init(b_odone, 1);
     ptx::mbar_init(b_final, 1);
@@ -264,7 +290,6 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
         ptx::tma_load_3d(s_q + hf * kBoxBytes, &p.tm_q, b_q, hf * 64, head, wk.q_start + q0);
     }
     int k_issued = 0, v_issued = 0;
-    bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
       const int s = t % kStages;
       const uint32_t ph = (t / kStages) & 1;
@@ -290,8 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
 #pragma unroll
         for (int i = 0; i < 8; ++i) blk_ids[i] = __shfl_sync(0xffffffffu, blk, i);
       }
-      ok = __all_sync(0xffffffffu, wait_bar(b_kempty(s), ph ^ 1, abort_flag, kErrWaitProducer));
-      if (!ok) break;
+      if (!__all_sync(0xffffffffu, wait_bar(b_kempty(s), ph ^ 1, abort_flag, kErrWaitProducer)))
+        break;
       if (lane == 0) {
         ptx::mbar_arrive_expect_tx(b_kfull(s), kTileBytes);
         if (paged) {
@@ -306,8 +331,8 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
         }
       }
       k_issued = t + 1;
-      ok = __all_sync(0xffffffffu, wait_bar(b_vempty(s), ph ^ 1, abort_flag, kErrWaitProducer));
-      if (!ok) break;
+      if (!__all_sync(0xffffffffu, wait_bar(b_vempty(s), ph ^ 1, abort_flag, kErrWaitProducer)))
+        break;
       if (lane == 0) {
         ptx::mbar_arrive_expect_tx(b_vfull(s), kTileBytes);
         if (paged) {
@@ -348,7 +373,15 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
 #pragma unroll
         for (int kk = 0; kk < kBlockN / 16; ++kk) {
           const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
-          ptx::umma_ts(tmem + 256, tmem + b * 128 + kk * 8, bdesc, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+          ptx::umma_ts(tmem + 256, tmem + b * 128 + kk * 8, bdesc, kIdescPV,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (precise) {
+#pragma unroll
+          for (int kk = 0; kk < kBlockN / 16; ++kk) {
+            const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
+            ptx::umma_ts(tmem + 256, tmem + b * 128 + 64 + kk * 8, bdesc, kIdescPV, 1u);
+          }
         }
         ptx::umma_commit(b_vempty(s));
         ptx::umma_commit(b_odone);
@@ -385,12 +418,15 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     drain_bar(b_final, 0);
   } else {
     // ================================================================ softmax + epilogue
-    const int row = warp * 32 + lane;  // == TMEM lane
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const int qrow = q0 + row;         // work-item-relative query row
+    const int quarter = warp & 3;
+    const int half = warp >> 2;                  // which 64 keys of each S tile / D/2 of O
+    const int row = quarter * 32 + lane;         // == TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int qrow = q0 + row;                   // work-item-relative query row
     const float scale_log2 = p.scale_log2;
-    float m_used = -INFINITY;  // running max, base-2 scaled domain
-    float l = 0.f;
+    constexpr int kOHalf = D / 2;                // O columns owned by this thread
+    float m_used = -INFINITY;  // running max of the row, base-2 scaled domain
+    float l = 0.f;             // this thread's share of the row sum
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
       const int b = t & 1;
@@ -398,51 +434,74 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       if (!ok) break;
       ptx::tc_fence_after();
       const int sg = t < tiles0 ? 0 : 1;
-      const int key0 = (sg == 0 ? t : t - tiles0) * kBlockN;
+      const int key0 = (sg == 0 ? t : t - tiles0) * kBlockN + half * 64;
       const hcp_kv_segment& seg = wk.seg[sg];
       int vis = seg.len - key0;
       if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
-      vis = max(0, min(vis, kBlockN));
+      vis = max(0, min(vis, 64));
 
-      uint32_t sr[128];
-      const uint32_t s_addr = tmem + lane_base + b * 128;
+      uint32_t sr[64];
+      const uint32_t s_addr = tmem + lane_base + b * 128 + half * 64;
       ptx::tmem_ld_32x32b_x32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
       ptx::tmem_ld_32x32b_x32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-      ptx::tmem_ld_32x32b_x32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[64]));
-      ptx::tmem_ld_32x32b_x32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&sr[96]));
       ptx::tmem_wait_ld();
 
       float mx = -INFINITY;
-      if (vis >= kBlockN) {
+      if (vis >= 64) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
+        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < 64; ++i) {
           const float x = i < vis ? __uint_as_float(sr[i]) : -INFINITY;
           sr[i] = __float_as_uint(x);
           mx = fmaxf(mx, x);
         }
       }
+      // exchange the partial max with the other half of the row
+      float* red_t = red + (t & 1) * 256;
+      red_t[half * 128 + row] = mx;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(b_red(b));
+      ok = __all_sync(0xffffffffu, wait_bar(b_red(b), (t >> 1) & 1, abort_flag, kErrWaitSoftmax));
+      if (!ok) break;
+      mx = fmaxf(mx, red_t[(half ^ 1) * 128 + row]);
+
       const float mx2 = mx * scale_log2;  // -inf stays -inf
       const bool raise = mx2 > m_used + kRescaleThreshold;
       const float m_new = raise ? mx2 : m_used;
       const float alpha = raise ? ex2_approx(m_used - m_new) : 1.f;  // 0 when m_used = -inf
       const float m_base = (m_new == -INFINITY) ? 0.f : m_new;
       float sum0 = 0.f, sum1 = 0.f;
-      uint32_t pk[64];
+      uint32_t pk[32];
+      const uint32_t p_addr = tmem + lane_base + b * 128 + half * 32;
+      if (!precise) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), scale_log2, -m_base));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, -m_base));
-        sum0 += p0;
-        sum1 += p1;
-        pk[i] = pack2<F16>(p0, p1);
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), scale_log2, -m_base));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, -m_base));
+          sum0 += p0;
+          sum1 += p1;
+          pk[i] = pack2<F16>(p0, p1);
+        }
+        ptx::tmem_st_32x32b_x32(p_addr, pk);
+      } else {
+        uint32_t pl[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), scale_log2, -m_base));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, -m_base));
+          sum0 += p0;
+          sum1 += p1;
+          pk[i] = pack2<F16>(p0, p1);
+          const float2 hi2 = unpack2<F16>(pk[i]);
+          pl[i] = pack2<F16>(p0 - hi2.x, p1 - hi2.y);
+        }
+        ptx::tmem_st_32x32b_x32(p_addr, pk);
+        ptx::tmem_st_32x32b_x32(p_addr + 64, pl);
       }
       l = l * alpha + (sum0 + sum1);
       m_used = m_new;
-      ptx::tmem_st_32x32b_x32(s_addr + 0, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-      ptx::tmem_st_32x32b_x32(s_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
 
       if (t >= 1) {
         // O += P_{t-1} V_{t-1} must have landed before O is rescaled and
@@ -451,9 +510,9 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
         if (!ok) break;
         ptx::tc_fence_after();
         if (__any_sync(0xffffffffu, raise)) {
-          const uint32_t o_addr = tmem + lane_base + 256;
+          const uint32_t o_addr = tmem + lane_base + 256 + half * kOHalf;
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < kOHalf / 32; ++c) {
             uint32_t o[32];
             ptx::tmem_ld_32x32b_x32(o_addr + c * 32, o);
             ptx::tmem_wait_ld();
@@ -471,22 +530,33 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     if (ok && n_tiles > 0) {
       ok = __all_sync(0xffffffffu, wait_bar(b_odone, (n_tiles - 1) & 1, abort_flag, kErrWaitSoftmax));
       ptx::tc_fence_after();
+      if (ok) {
+        // combine the two halves' row sums (same exchange as the row max)
+        const int b = n_tiles & 1;
+        float* red_t = red + b * 256;
+        red_t[half * 128 + row] = l;
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(b_red(b));
+        ok = __all_sync(0xffffffffu,
+                        wait_bar(b_red(b), (n_tiles >> 1) & 1, abort_flag, kErrWaitSoftmax));
+        if (ok) l += red_t[(half ^ 1) * 128 + row];
+      }
     }
     if (ok) {
       // ---------------------------------------------------------- epilogue
-      float o[D];
+      float o[kOHalf];
       if (n_tiles > 0) {
-        uint32_t ob[D];
-        const uint32_t o_addr = tmem + lane_base + 256;
+        uint32_t ob[kOHalf];
+        const uint32_t o_addr = tmem + lane_base + 256 + half * kOHalf;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c)
+        for (int c = 0; c < kOHalf / 32; ++c)
           ptx::tmem_ld_32x32b_x32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ob[c * 32]));
         ptx::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < D; ++i) o[i] = __uint_as_float(ob[i]);
+        for (int i = 0; i < kOHalf; ++i) o[i] = __uint_as_float(ob[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < D; ++i) o[i] = 0.f;
+        for (int i = 0; i < kOHalf; ++i) o[i] = 0.f;
       }
       const bool valid = qrow < wk.q_len;
       if (valid) {
@@ -496,6 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
         float f_old = 0.f;
         const long long out_row = static_cast<long long>(wk.q_start) + qrow;
         const long long lse_idx_col = static_cast<long long>(wk.lse_col) + qrow;
+        const long long col0 = static_cast<long long>(head) * D + half * kOHalf;
         if (p.merge_lse != nullptr) {
           float lp = p.merge_lse[head * p.merge_lse_stride + lse_idx_col];
           if (lp == INFINITY) lp = -INFINITY;
@@ -512,11 +583,12 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
             f_new *= wn * inv;
             lse_v = mm + __logf(wp + wn);
           }
-          const long long base = out_row * p.merge_o_row_stride + static_cast<long long>(head) * D;
+          const long long base = out_row * p.merge_o_row_stride + col0;
           if (p.merge_o_f32) {
-            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.merge_o) + base);
+            const float4* src =
+                reinterpret_cast<const float4*>(static_cast<const float*>(p.merge_o) + base);
 #pragma unroll
-            for (int c = 0; c < D / 4; ++c) {
+            for (int c = 0; c < kOHalf / 4; ++c) {
               const float4 v = src[c];
               o[4 * c + 0] = o[4 * c + 0] * f_new + v.x * f_old;
               o[4 * c + 1] = o[4 * c + 1] * f_new + v.y * f_old;
@@ -524,9 +596,10 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
               o[4 * c + 3] = o[4 * c + 3] * f_new + v.w * f_old;
             }
           } else {
-            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.merge_o) + base);
+            const uint4* src =
+                reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.merge_o) + base);
 #pragma unroll
-            for (int c = 0; c < D / 8; ++c) {
+            for (int c = 0; c < kOHalf / 8; ++c) {
               const uint4 v = src[c];
               const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -539,22 +612,23 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < D; ++i) o[i] *= f_new;
+          for (int i = 0; i < kOHalf; ++i) o[i] *= f_new;
         }
-        const long long obase = out_row * p.out_row_stride + static_cast<long long>(head) * D;
+        const long long obase = out_row * p.out_row_stride + col0;
         if (p.out_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase);
 #pragma unroll
-          for (int c = 0; c < D / 4; ++c)
+          for (int c = 0; c < kOHalf / 4; ++c)
             dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
         } else {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + obase);
 #pragma unroll
-          for (int c = 0; c < D / 8; ++c)
+          for (int c = 0; c < kOHalf / 8; ++c)
             dst[c] = make_uint4(pack2<F16>(o[8 * c], o[8 * c + 1]), pack2<F16>(o[8 * c + 2], o[8 * c + 3]),
-                                pack2<F16>(o[8 * c + 4], o[8 * c + 5]), pack2<F16>(o[8 * c + 6], o[8 * c + 7]));
+                                pack2<F16>(o[8 * c + 4], o[8 * c + 5]),
+                                pack2<F16>(o[8 * c + 6], o[8 * c + 7]));
         }
-        if (p.lse != nullptr) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
+        if (p.lse != nullptr && half == 0) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
       }
     }
   }
@@ -570,8 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
 
 template <int D>
 constexpr int fwd_smem_bytes() {
-  return 1024 /* alignment slack */ + (D / 64) * 128 * 128 * (1 + 2 * kStages) +
-         8 * (7 + 4 * kStages) + 16;
+  return FwdSmem<D>::kBytes;
 }
 
 }  // namespace hcp
