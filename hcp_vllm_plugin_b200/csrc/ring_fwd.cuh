@@ -8,28 +8,29 @@
 // separate merge kernel.
 //
 // Warp roles (320 threads):
-//   warps 0-7  softmax / O correction / epilogue.  Query row r of the tile is
-//              TMEM lane r; warp w handles lanes 32*(w%4).. and key/column half
-//              w/4 of every S tile (two threads per row, which keeps two
-//              softmax warps per SM sub-partition in flight).  The two halves
-//              of a row exchange their partial row max through shared memory
-//              once per KV tile (bounded mbarrier, never bar.sync).
+//   warps 0-7  two softmax warpgroups.  Warpgroup g (warps 4g..4g+3) owns
+//              the KV tiles t with t % 2 == g: it keeps its own online-softmax
+//              state (running max, row sum) and its own O accumulator, so the
+//              two warps that share an SM sub-partition work on different
+//              tiles, out of phase.  Thread (w, lane) owns query row
+//              32*(w%4)+lane, which is TMEM lane 32*(w%4)+lane.  The two
+//              partial results are merged once, in the epilogue.
 //   warp 8     TMA producer: Q once, then K and V tiles through a 2-stage ring
 //              (contiguous 3-D tensor maps, or 4-D maps over the paged cache
 //              indexed through the block table)
 //   warp 9     tcgen05 MMA issuer (one lane) and TMEM owner
 //
 // TMEM (512 columns x 128 lanes, fp32):
-//   [  0,128)  S buffer 0      S = Q K^T of even KV tiles.  P (16-bit, two keys
-//   [128,256)  S buffer 1      per column) is written back over columns 0-63 and
-//                              feeds O += P V as the A operand; for short rows
-//                              the low part P - bf16(P) goes to columns 64-127
-//                              and is accumulated by a second PV product
-//   [256,256+D) O accumulator
+//   [  0,128)      S_0 = Q K^T of even KV tiles, [128,256) S_1 of odd tiles.
+//                  P (16-bit, two keys per column) is written back over
+//                  columns 0-63 of its S buffer and feeds O_g += P V as the A
+//                  operand; for short rows the low part P - bf16(P) goes to
+//                  columns 64-127 and is accumulated by a second PV product.
+//   [256,256+D)    O_0 (even tiles), [256+D, 256+2D) O_1 (odd tiles)
 //
 // Shared memory (1024-byte aligned, 128-byte swizzle, 64-element boxes):
-//   Q tile, then per stage a K tile and a V tile, then the row-max exchange
-//   buffers and the mbarriers.
+//   Q tile, then per stage a K tile and a V tile, then the epilogue exchange
+//   buffer and the mbarriers.
 //
 // Numerics: scores are scaled into the base-2 domain (scale * log2 e), the
 // running max is only raised when a tile's max exceeds it by more than 8
@@ -214,8 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   auto b_vempty = [&](int s) { return bar0 + 8u * (1 + 3 * kStages + s); };
   auto b_sfull = [&](int b) { return bar0 + 8u * (1 + 4 * kStages + b); };
   auto b_pfull = [&](int b) { return bar0 + 8u * (3 + 4 * kStages + b); };
-  auto b_red = [&](int b) { return bar0 + 8u * (5 + 4 * kStages + b); };
-  const uint32_t b_odone = bar0 + 8u * (7 + 4 * kStages);
+  auto b_odone = [&](int b) { return bar0 + 8u * (5 + 4 * kStages + b); };
+  const uint32_t b_red = bar0 + 8u * (7 + 4 * kStages);
   const uint32_t b_final = bar0 + 8u * (8 + 4 * kStages);
 
   const int warp = threadIdx.x >> 5;
@@ -255,10 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(b_sfull(b), 1);
-      ptx::mbar_init(b_pfull(b), kSoftmaxThreads);
-      ptx::mbar_init(b_red(b), kSoftmaxWarps);
+      ptx::mbar_init(b_pfull(b), kSoftmaxThreads / 2);
+      ptx::mbar_init(b_odone(b), 1);
     }
-    ptx::mbar_init(b_odone, 1);
+    ptx::mbar_init(b_red, kSoftmaxWarps);
     ptx::mbar_init(b_final, 1);
     // A CTA starting after another one failed does no work.
     *abort_flag = *reinterpret_cast<volatile int*>(&g_device_status) != 0 ? 1 : 0;
@@ -371,20 +372,20 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       if (lane == 0) {
         const uint32_t s_v = s_kv0 + (2 * s + 1) * kTileBytes;
 #pragma unroll
+        const uint32_t o_acc = tmem + 256 + b * D;  // O_b accumulates the tiles of parity b
         for (int kk = 0; kk < kBlockN / 16; ++kk) {
           const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
-          ptx::umma_ts(tmem + 256, tmem + b * 128 + kk * 8, bdesc, kIdescPV,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+          ptx::umma_ts(o_acc, tmem + b * 128 + kk * 8, bdesc, kIdescPV, (j >= 2 || kk > 0) ? 1u : 0u);
         }
         if (precise) {
 #pragma unroll
           for (int kk = 0; kk < kBlockN / 16; ++kk) {
             const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
-            ptx::umma_ts(tmem + 256, tmem + b * 128 + 64 + kk * 8, bdesc, kIdescPV, 1u);
+            ptx::umma_ts(o_acc, tmem + b * 128 + 64 + kk * 8, bdesc, kIdescPV, 1u);
           }
         }
         ptx::umma_commit(b_vempty(s));
-        ptx::umma_commit(b_odone);
+        ptx::umma_commit(b_odone(b));
       }
       __syncwarp();
       return true;
@@ -418,218 +419,223 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     drain_bar(b_final, 0);
   } else {
     // ================================================================ softmax + epilogue
+    const int g = warp >> 2;                 // warpgroup: KV tiles t with t % 2 == g
     const int quarter = warp & 3;
-    const int half = warp >> 2;                  // which 64 keys of each S tile / D/2 of O
-    const int row = quarter * 32 + lane;         // == TMEM lane
+    const int row = quarter * 32 + lane;     // == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int qrow = q0 + row;                   // work-item-relative query row
+    const int qrow = q0 + row;               // work-item-relative query row
     const float scale_log2 = p.scale_log2;
-    constexpr int kOHalf = D / 2;                // O columns owned by this thread
-    float m_used = -INFINITY;  // running max of the row, base-2 scaled domain
-    float l = 0.f;             // this thread's share of the row sum
+    const uint32_t s_addr = tmem + lane_base + g * 128;
+    const uint32_t o_own = tmem + lane_base + 256 + g * D;
+    constexpr int kOHalf = D / 2;            // output columns this thread writes
+    float m_used = -INFINITY;  // running max over this warpgroup's tiles, base-2 scaled domain
+    float l = 0.f;             // row sum over this warpgroup's tiles
     bool ok = true;
-    for (int t = 0; t < n_tiles; ++t) {
-      const int b = t & 1;
-      ok = __all_sync(0xffffffffu, wait_bar(b_sfull(b), (t >> 1) & 1, abort_flag, kErrWaitSoftmax));
+    int my_tiles = 0;
+    for (int t = g; t < n_tiles; t += 2) {
+      ok = __all_sync(0xffffffffu, wait_bar(b_sfull(g), (t >> 1) & 1, abort_flag, kErrWaitSoftmax));
       if (!ok) break;
       ptx::tc_fence_after();
       const int sg = t < tiles0 ? 0 : 1;
-      const int key0 = (sg == 0 ? t : t - tiles0) * kBlockN + half * 64;
+      const int key0 = (sg == 0 ? t : t - tiles0) * kBlockN;
       const hcp_kv_segment& seg = wk.seg[sg];
       int vis = seg.len - key0;
       if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
-      vis = max(0, min(vis, 64));
+      vis = max(0, min(vis, kBlockN));
 
-      uint32_t sr[64];
-      const uint32_t s_addr = tmem + lane_base + b * 128 + half * 64;
-      ptx::tmem_ld_32x32b_x32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-      ptx::tmem_ld_32x32b_x32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+      uint32_t sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        ptx::tmem_ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       ptx::tmem_wait_ld();
-
-      float mx = -INFINITY;
-      if (vis >= 64) {
+      if (vis < kBlockN) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const float x = i < vis ? __uint_as_float(sr[i]) : -INFINITY;
-          sr[i] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
+        for (int i = 0; i < 128; ++i)
+          if (i >= vis) sr[i] = __float_as_uint(-INFINITY);
       }
-      // exchange the partial max with the other half of the row
-      float* red_t = red + (t & 1) * 256;
-      red_t[half * 128 + row] = mx;
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(b_red(b));
-      ok = __all_sync(0xffffffffu, wait_bar(b_red(b), (t >> 1) & 1, abort_flag, kErrWaitSoftmax));
-      if (!ok) break;
-      mx = fmaxf(mx, red_t[(half ^ 1) * 128 + row]);
-
+      float mx8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx8[j] = __uint_as_float(sr[j]);
+#pragma unroll
+      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mx2 = mx * scale_log2;  // -inf stays -inf
       const bool raise = mx2 > m_used + kRescaleThreshold;
       const float m_new = raise ? mx2 : m_used;
       const float alpha = raise ? ex2_approx(m_used - m_new) : 1.f;  // 0 when m_used = -inf
       const float m_base = (m_new == -INFINITY) ? 0.f : m_new;
-      float sum0 = 0.f, sum1 = 0.f;
-      uint32_t pk[32];
-      const uint32_t p_addr = tmem + lane_base + b * 128 + half * 32;
+      float sums[4] = {0.f, 0.f, 0.f, 0.f};
       if (!precise) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), scale_log2, -m_base));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, -m_base));
-          sum0 += p0;
-          sum1 += p1;
-          pk[i] = pack2<F16>(p0, p1);
-        }
-        ptx::tmem_st_32x32b_x32(p_addr, pk);
-      } else {
-        uint32_t pl[32];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), scale_log2, -m_base));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), scale_log2, -m_base));
-          sum0 += p0;
-          sum1 += p1;
-          pk[i] = pack2<F16>(p0, p1);
-          const float2 hi2 = unpack2<F16>(pk[i]);
-          pl[i] = pack2<F16>(p0 - hi2.x, p1 - hi2.y);
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
+            const float p1 =
+                ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+            sums[i & 3] += p0 + p1;
+            pk[i] = pack2<F16>(p0, p1);
+          }
+          ptx::tmem_st_32x32b_x16(s_addr + c * 16, pk);
         }
-        ptx::tmem_st_32x32b_x32(p_addr, pk);
-        ptx::tmem_st_32x32b_x32(p_addr + 64, pl);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16], pl[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
+            const float p1 =
+                ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+            sums[i & 3] += p0 + p1;
+            pk[i] = pack2<F16>(p0, p1);
+            const float2 h2 = unpack2<F16>(pk[i]);
+            pl[i] = pack2<F16>(p0 - h2.x, p1 - h2.y);
+          }
+          ptx::tmem_st_32x32b_x16(s_addr + c * 16, pk);
+          ptx::tmem_st_32x32b_x16(s_addr + 64 + c * 16, pl);
+        }
       }
-      l = l * alpha + (sum0 + sum1);
+      l = l * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
       m_used = m_new;
 
-      if (t >= 1) {
-        // O += P_{t-1} V_{t-1} must have landed before O is rescaled and
-        // before P_t is released to the MMA warp.
-        ok = __all_sync(0xffffffffu, wait_bar(b_odone, (t - 1) & 1, abort_flag, kErrWaitSoftmax));
+      if (my_tiles >= 1) {
+        // O_g += P V of this warpgroup's previous tile must have landed before
+        // O_g is rescaled and before this P is released to the MMA warp.
+        ok = __all_sync(0xffffffffu,
+                        wait_bar(b_odone(g), (my_tiles - 1) & 1, abort_flag, kErrWaitSoftmax));
         if (!ok) break;
         ptx::tc_fence_after();
         if (__any_sync(0xffffffffu, raise)) {
-          const uint32_t o_addr = tmem + lane_base + 256 + half * kOHalf;
 #pragma unroll
-          for (int c = 0; c < kOHalf / 32; ++c) {
+          for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
-            ptx::tmem_ld_32x32b_x32(o_addr + c * 32, o);
+            ptx::tmem_ld_32x32b_x32(o_own + c * 32, o);
             ptx::tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            ptx::tmem_st_32x32b_x32(o_addr + c * 32, o);
+            ptx::tmem_st_32x32b_x32(o_own + c * 32, o);
           }
         }
       }
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(b_pfull(b));
+      ptx::mbar_arrive(b_pfull(g));
+      ++my_tiles;
     }
-
-    if (ok && n_tiles > 0) {
-      ok = __all_sync(0xffffffffu, wait_bar(b_odone, (n_tiles - 1) & 1, abort_flag, kErrWaitSoftmax));
+    if (ok && my_tiles > 0) {
+      ok = __all_sync(0xffffffffu,
+                      wait_bar(b_odone(g), (my_tiles - 1) & 1, abort_flag, kErrWaitSoftmax));
       ptx::tc_fence_after();
-      if (ok) {
-        // combine the two halves' row sums (same exchange as the row max)
-        const int b = n_tiles & 1;
-        float* red_t = red + b * 256;
-        red_t[half * 128 + row] = l;
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(b_red(b));
-        ok = __all_sync(0xffffffffu,
-                        wait_bar(b_red(b), (n_tiles >> 1) & 1, abort_flag, kErrWaitSoftmax));
-        if (ok) l += red_t[(half ^ 1) * 128 + row];
-      }
+    }
+    // exchange (running max, row sum) with the other warpgroup; its O buffer
+    // is complete once it has arrived here
+    float2* xch = reinterpret_cast<float2*>(red);  // [2][128]
+    if (ok) {
+      xch[g * 128 + row] = make_float2(m_used, l);
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(b_red);
+      ok = __all_sync(0xffffffffu, wait_bar(b_red, 0, abort_flag, kErrWaitSoftmax));
+      ptx::tc_fence_after();
     }
     if (ok) {
       // ---------------------------------------------------------- epilogue
-      float o[kOHalf];
-      if (n_tiles > 0) {
-        uint32_t ob[kOHalf];
-        const uint32_t o_addr = tmem + lane_base + 256 + half * kOHalf;
-#pragma unroll
-        for (int c = 0; c < kOHalf / 32; ++c)
-          ptx::tmem_ld_32x32b_x32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ob[c * 32]));
-        ptx::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < kOHalf; ++i) o[i] = __uint_as_float(ob[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < kOHalf; ++i) o[i] = 0.f;
+      const float2 other = xch[(g ^ 1) * 128 + row];
+      const float m0 = g == 0 ? m_used : other.x, l0 = g == 0 ? l : other.y;
+      const float m1 = g == 0 ? other.x : m_used, l1 = g == 0 ? other.y : l;
+      const float mm2 = fmaxf(m0, m1);
+      float f0 = 0.f, f1 = 0.f, lsum = 0.f;
+      if (mm2 != -INFINITY) {
+        f0 = l0 > 0.f ? ex2_approx(m0 - mm2) : 0.f;
+        f1 = l1 > 0.f ? ex2_approx(m1 - mm2) : 0.f;
+        lsum = l0 * f0 + l1 * f1;
       }
       const bool valid = qrow < wk.q_len;
-      if (valid) {
-        const float LN2 = 0.69314718055994530942f;
-        float lse_v = (l > 0.f) ? (m_used + lg2_approx(l)) * LN2 : -INFINITY;
-        float f_new = (l > 0.f) ? 1.f / l : 0.f;
-        float f_old = 0.f;
-        const long long out_row = static_cast<long long>(wk.q_start) + qrow;
-        const long long lse_idx_col = static_cast<long long>(wk.lse_col) + qrow;
-        const long long col0 = static_cast<long long>(head) * D + half * kOHalf;
-        if (p.merge_lse != nullptr) {
-          float lp = p.merge_lse[head * p.merge_lse_stride + lse_idx_col];
-          if (lp == INFINITY) lp = -INFINITY;
-          const float mm = fmaxf(lp, lse_v);
-          if (mm == -INFINITY) {
-            f_new = 0.f;
-            f_old = 0.f;
-            lse_v = -INFINITY;
-          } else {
-            const float wp = __expf(lp - mm);
-            const float wn = __expf(lse_v - mm);
-            const float inv = 1.f / (wp + wn);
-            f_old = wp * inv;
-            f_new *= wn * inv;
-            lse_v = mm + __logf(wp + wn);
-          }
-          const long long base = out_row * p.merge_o_row_stride + col0;
-          if (p.merge_o_f32) {
-            const float4* src =
-                reinterpret_cast<const float4*>(static_cast<const float*>(p.merge_o) + base);
+      const float LN2 = 0.69314718055994530942f;
+      float lse_v = (lsum > 0.f) ? (mm2 + lg2_approx(lsum)) * LN2 : -INFINITY;
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      f0 *= inv;
+      f1 *= inv;
+      float f_old = 0.f;
+      const long long out_row = static_cast<long long>(wk.q_start) + qrow;
+      const long long lse_idx_col = static_cast<long long>(wk.lse_col) + qrow;
+      const bool merging = p.merge_lse != nullptr;
+      if (merging && valid) {
+        float lp = p.merge_lse[head * p.merge_lse_stride + lse_idx_col];
+        if (lp == INFINITY) lp = -INFINITY;
+        const float mm = fmaxf(lp, lse_v);
+        if (mm == -INFINITY) {
+          f0 = f1 = 0.f;
+          lse_v = -INFINITY;
+        } else {
+          const float wp = __expf(lp - mm);
+          const float wn = __expf(lse_v - mm);
+          const float r = 1.f / (wp + wn);
+          f_old = wp * r;
+          f0 *= wn * r;
+          f1 *= wn * r;
+          lse_v = mm + __logf(wp + wn);
+        }
+      }
+      const bool have0 = n_tiles >= 1, have1 = n_tiles >= 2;
+      const long long col0 = static_cast<long long>(head) * D + g * kOHalf;
 #pragma unroll
-            for (int c = 0; c < kOHalf / 4; ++c) {
-              const float4 v = src[c];
-              o[4 * c + 0] = o[4 * c + 0] * f_new + v.x * f_old;
-              o[4 * c + 1] = o[4 * c + 1] * f_new + v.y * f_old;
-              o[4 * c + 2] = o[4 * c + 2] * f_new + v.z * f_old;
-              o[4 * c + 3] = o[4 * c + 3] * f_new + v.w * f_old;
+      for (int c = 0; c < kOHalf / 32; ++c) {
+        uint32_t r0[32], r1[32];
+        if (have0) ptx::tmem_ld_32x32b_x32(tmem + lane_base + 256 + g * kOHalf + c * 32, r0);
+        if (have1) ptx::tmem_ld_32x32b_x32(tmem + lane_base + 256 + D + g * kOHalf + c * 32, r1);
+        ptx::tmem_wait_ld();
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          o[i] = (have0 ? __uint_as_float(r0[i]) * f0 : 0.f) + (have1 ? __uint_as_float(r1[i]) * f1 : 0.f);
+        if (!valid) continue;
+        if (merging) {
+          const long long base = out_row * p.merge_o_row_stride + col0 + c * 32;
+          if (p.merge_o_f32) {
+            const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.merge_o) + base);
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+              const float4 v = src[q4];
+              o[4 * q4 + 0] += v.x * f_old;
+              o[4 * q4 + 1] += v.y * f_old;
+              o[4 * q4 + 2] += v.z * f_old;
+              o[4 * q4 + 3] += v.w * f_old;
             }
           } else {
-            const uint4* src =
-                reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.merge_o) + base);
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.merge_o) + base);
 #pragma unroll
-            for (int c = 0; c < kOHalf / 8; ++c) {
-              const uint4 v = src[c];
+            for (int q8 = 0; q8 < 4; ++q8) {
+              const uint4 v = src[q8];
               const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 f = unpack2<F16>(w[e]);
-                o[8 * c + 2 * e] = o[8 * c + 2 * e] * f_new + f.x * f_old;
-                o[8 * c + 2 * e + 1] = o[8 * c + 2 * e + 1] * f_new + f.y * f_old;
+                o[8 * q8 + 2 * e] += f.x * f_old;
+                o[8 * q8 + 2 * e + 1] += f.y * f_old;
               }
             }
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < kOHalf; ++i) o[i] *= f_new;
         }
-        const long long obase = out_row * p.out_row_stride + col0;
+        const long long obase = out_row * p.out_row_stride + col0 + c * 32;
         if (p.out_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase);
 #pragma unroll
-          for (int c = 0; c < kOHalf / 4; ++c)
-            dst[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+          for (int q4 = 0; q4 < 8; ++q4)
+            dst[q4] = make_float4(o[4 * q4], o[4 * q4 + 1], o[4 * q4 + 2], o[4 * q4 + 3]);
         } else {
           uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + obase);
 #pragma unroll
-          for (int c = 0; c < kOHalf / 8; ++c)
-            dst[c] = make_uint4(pack2<F16>(o[8 * c], o[8 * c + 1]), pack2<F16>(o[8 * c + 2], o[8 * c + 3]),
-                                pack2<F16>(o[8 * c + 4], o[8 * c + 5]),
-                                pack2<F16>(o[8 * c + 6], o[8 * c + 7]));
+          for (int q8 = 0; q8 < 4; ++q8)
+            dst[q8] = make_uint4(pack2<F16>(o[8 * q8], o[8 * q8 + 1]), pack2<F16>(o[8 * q8 + 2], o[8 * q8 + 3]),
+                                 pack2<F16>(o[8 * q8 + 4], o[8 * q8 + 5]),
+                                 pack2<F16>(o[8 * q8 + 6], o[8 * q8 + 7]));
         }
-        if (p.lse != nullptr && half == 0) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
       }
+      if (valid && p.lse != nullptr && g == 0) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
     }
   }
 
