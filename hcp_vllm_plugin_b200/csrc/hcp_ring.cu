@@ -247,7 +247,7 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
     for (int i = 0; i < n; ++i) {
       p.work[i] = items[order[base + i]];
       p.tile_off[i] = tiles;
-      tiles += (p.work[i].q_len + kBlockM - 1) / kBlockM;
+      tiles += (p.work[i].q_len + kCtaRows - 1) / kCtaRows;
     }
     p.tile_off[n] = tiles;
     p.num_work = n;

@@ -1,36 +1,39 @@
 // Fused ring-attention forward for B200 (sm_100a).
 //
-// One CTA computes one 128-row query tile of one query head over the union
-// of up to two KV segments (the transient peer prefix, non-causal, and the
-// local chunk, causal at a global offset), with a single online softmax, and
-// writes the normalised output plus the per-row natural-log LSE.  An earlier
-// partial (O, LSE) can be merged in the epilogue, so ring hops chain without a
-// separate merge kernel.
+// One CTA computes 256 query rows (two 128-row tiles, "A" and "B") of one
+// query head over the union of up to two KV segments (the transient peer
+// prefix, non-causal, and the local chunk, causal at a global offset), with an
+// online softmax per row, and writes the normalised output plus the per-row
+// natural-log LSE.  An earlier partial (O, LSE) can be merged in the epilogue,
+// so ring hops chain without a separate merge kernel.
+//
+// Every K/V tile staged in shared memory feeds both query tiles: the kernel is
+// bound by operand traffic (L2 -> shared memory -> tensor core), and sharing
+// halves it per FLOP.
 //
 // Warp roles (320 threads):
-//   warps 0-7  two softmax warpgroups.  Warpgroup g (warps 4g..4g+3) owns
-//              the KV tiles t with t % 2 == g: it keeps its own online-softmax
-//              state (running max, row sum) and its own O accumulator, so the
-//              two warps that share an SM sub-partition work on different
-//              tiles, out of phase.  Thread (w, lane) owns query row
-//              32*(w%4)+lane, which is TMEM lane 32*(w%4)+lane.  The two
-//              partial results are merged once, in the epilogue.
-//   warp 8     TMA producer: Q once, then K and V tiles through a 2-stage ring
-//              (contiguous 3-D tensor maps, or 4-D maps over the paged cache
-//              indexed through the block table)
-//   warp 9     tcgen05 MMA issuer (one lane) and TMEM owner
+//   warps 0-3  softmax / O correction / epilogue of query tile A
+//   warps 4-7  the same for query tile B.  Thread (w, lane) owns row
+//              32*(w%4)+lane of its tile, which is that TMEM lane.
+//   warp 8     TMA producer: Q_A, Q_B once, then K and V tiles through a
+//              2-stage ring (contiguous 3-D tensor maps, or 4-D maps over the
+//              paged cache indexed through the block table)
+//   warp 9     tcgen05 MMA issuer (one lane) and TMEM owner.  Per KV tile it
+//              issues  O_A += P_A V (previous tile), S_A = Q_A K,
+//                      O_B += P_B V (previous tile), S_B = Q_B K,
+//              so the tensor core works for one warpgroup while the other
+//              computes its softmax.
 //
 // TMEM (512 columns x 128 lanes, fp32):
-//   [  0,128)      S_0 = Q K^T of even KV tiles, [128,256) S_1 of odd tiles.
-//                  P (16-bit, two keys per column) is written back over
-//                  columns 0-63 of its S buffer and feeds O_g += P V as the A
-//                  operand; for short rows the low part P - bf16(P) goes to
-//                  columns 64-127 and is accumulated by a second PV product.
-//   [256,256+D)    O_0 (even tiles), [256+D, 256+2D) O_1 (odd tiles)
+//   [  0,128)      S_A,  [128,256) S_B.  P (16-bit, two keys per column) is
+//                  written back over columns 0-63 of its S buffer and feeds
+//                  O += P V as the A operand; for rows that see few keys the
+//                  low part P - bf16(P) goes to columns 64-127 and is
+//                  accumulated by a second PV product.
+//   [256,256+D)    O_A,  [256+D, 256+2D) O_B
 //
 // Shared memory (1024-byte aligned, 128-byte swizzle, 64-element boxes):
-//   Q tile, then per stage a K tile and a V tile, then the epilogue exchange
-//   buffer and the mbarriers.
+//   Q_A, Q_B, then per stage a K tile and a V tile, then the mbarriers.
 //
 // Numerics: scores are scaled into the base-2 domain (scale * log2 e), the
 // running max is only raised when a tile's max exceeds it by more than 8
@@ -48,11 +51,10 @@ namespace hcp {
 
 __device__ int g_device_status = 0;
 
-constexpr int kBlockM = 128;
-constexpr int kBlockN = 128;
+constexpr int kBlockM = 128;          // rows per query tile (one TMEM lane each)
+constexpr int kCtaRows = 2 * kBlockM;  // query rows per CTA
+constexpr int kBlockN = 128;          // keys per KV tile
 constexpr int kStages = 2;
-constexpr int kSoftmaxWarps = 8;
-constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
 constexpr int kThreads = 320;
@@ -171,7 +173,7 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
 
 // Keys of segment `sg` visible to the valid rows [q0, q0+rows) of a query tile.
 __device__ __forceinline__ int segment_keys(const hcp_kv_segment& sg, int q0, int rows) {
-  if (sg.src == HCP_SRC_NONE || sg.len <= 0) return 0;
+  if (rows <= 0 || sg.src == HCP_SRC_NONE || sg.len <= 0) return 0;
   if (sg.causal_off < 0) return sg.len;
   const long long last_visible = static_cast<long long>(sg.causal_off) + q0 + rows;  // exclusive
   return static_cast<int>(max(0ll, min(static_cast<long long>(sg.len), last_visible)));
@@ -181,9 +183,9 @@ template <int D>
 struct FwdSmem {
   static constexpr int kBoxBytes = 128 * 128;  // 128 rows x 64 elems x 2 B
   static constexpr int kTileBytes = (D / 64) * kBoxBytes;
-  static constexpr int kNumBars = 9 + 4 * kStages;
-  static constexpr int kRedOff = kTileBytes * (1 + 2 * kStages);  // float red[2][2][128]
-  static constexpr int kBarOff = kRedOff + 2 * 2 * 128 * 4;
+  static constexpr int kNumBars = 8 + 4 * kStages;
+  static constexpr int kKvOff = 2 * kTileBytes;                    // after Q_A, Q_B
+  static constexpr int kBarOff = kKvOff + 2 * kStages * kTileBytes;
   static constexpr int kEnd = kBarOff + 8 * kNumBars + 16;
   static constexpr int kBytes = kEnd + 1024;  // + alignment slack
 };
@@ -201,9 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const uint32_t s_q = ptx::smem_u32(smem);
-  const uint32_t s_kv0 = s_q + kTileBytes;  // stage s: K at +2s tiles, V at +2s+1 tiles
-  float* red = reinterpret_cast<float*>(smem + L::kRedOff);
+  const uint32_t s_q = ptx::smem_u32(smem);           // Q_A at s_q, Q_B at s_q + kTileBytes
+  const uint32_t s_kv0 = s_q + L::kKvOff;             // stage s: K at +2s tiles, V at +2s+1
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -213,16 +214,15 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   auto b_kempty = [&](int s) { return bar0 + 8u * (1 + kStages + s); };
   auto b_vfull = [&](int s) { return bar0 + 8u * (1 + 2 * kStages + s); };
   auto b_vempty = [&](int s) { return bar0 + 8u * (1 + 3 * kStages + s); };
-  auto b_sfull = [&](int b) { return bar0 + 8u * (1 + 4 * kStages + b); };
-  auto b_pfull = [&](int b) { return bar0 + 8u * (3 + 4 * kStages + b); };
-  auto b_odone = [&](int b) { return bar0 + 8u * (5 + 4 * kStages + b); };
-  const uint32_t b_red = bar0 + 8u * (7 + 4 * kStages);
-  const uint32_t b_final = bar0 + 8u * (8 + 4 * kStages);
+  auto b_sfull = [&](int x) { return bar0 + 8u * (1 + 4 * kStages + x); };
+  auto b_pfull = [&](int x) { return bar0 + 8u * (3 + 4 * kStages + x); };
+  auto b_odone = [&](int x) { return bar0 + 8u * (5 + 4 * kStages + x); };
+  const uint32_t b_final = bar0 + 8u * (7 + 4 * kStages);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- which (work item, query tile, head) this CTA owns
+  // ---- which (work item, 256-row block, head) this CTA owns
   const int H = p.num_heads;
   const int tile_global = blockIdx.x / H;
   const int head = blockIdx.x - tile_global * H;
@@ -233,17 +233,28 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     if (p.tile_off[mid] <= tile_global) lo = mid; else hi = mid - 1;
   }
   const hcp_attn_work& wk = p.work[lo];
-  const int n_qtiles = (wk.q_len + kBlockM - 1) / kBlockM;
-  const int m_tile = n_qtiles - 1 - (tile_global - p.tile_off[lo]);  // heaviest (last) tile first
-  const int q0 = m_tile * kBlockM;
-  const int rows_valid = min(kBlockM, wk.q_len - q0);
-  const int keys0 = segment_keys(wk.seg[0], q0, rows_valid);
-  const int keys1 = segment_keys(wk.seg[1], q0, rows_valid);
-  const int tiles0 = (keys0 + kBlockN - 1) / kBlockN;
-  const int n_tiles = tiles0 + (keys1 + kBlockN - 1) / kBlockN;
+  const int n_blocks = (wk.q_len + kCtaRows - 1) / kCtaRows;
+  const int m_blk = n_blocks - 1 - (tile_global - p.tile_off[lo]);  // heaviest (last) first
+  const int q0 = m_blk * kCtaRows;
+  const int rows_a = max(0, min(kBlockM, wk.q_len - q0));
+  const int rows_b = max(0, min(kBlockM, wk.q_len - q0 - kBlockM));
+  // keys each query tile needs from each segment; the KV tile list covers both
+  const int ka0 = segment_keys(wk.seg[0], q0, rows_a), kb0 = segment_keys(wk.seg[0], q0 + kBlockM, rows_b);
+  const int ka1 = segment_keys(wk.seg[1], q0, rows_a), kb1 = segment_keys(wk.seg[1], q0 + kBlockM, rows_b);
+  const int tiles0 = (max(ka0, kb0) + kBlockN - 1) / kBlockN;
+  const int n_tiles = tiles0 + (max(ka1, kb1) + kBlockN - 1) / kBlockN;
+  auto tile_seg = [&](int t) { return t < tiles0 ? 0 : 1; };
+  auto tile_key0 = [&](int t) { return (t < tiles0 ? t : t - tiles0) * kBlockN; };
+  // is KV tile t needed by query tile x (0 = A, 1 = B)?
+  auto active = [&](int x, int t) {
+    const int k0 = tile_key0(t);
+    const int need = tile_seg(t) == 0 ? (x == 0 ? ka0 : kb0) : (x == 0 ? ka1 : kb1);
+    return k0 < need;
+  };
   // Rows that see few keys in total get P as hi + lo 16-bit parts.
-  const bool precise =
-      segment_keys(wk.seg[0], q0, 1) + segment_keys(wk.seg[1], q0, 1) < kPreciseKeys;
+  const bool precise_a = segment_keys(wk.seg[0], q0, 1) + segment_keys(wk.seg[1], q0, 1) < kPreciseKeys;
+  const bool precise_b = segment_keys(wk.seg[0], q0 + kBlockM, 1) +
+                             segment_keys(wk.seg[1], q0 + kBlockM, 1) < kPreciseKeys;
 
   // ---- setup
   if (threadIdx.x == 0) {
@@ -254,12 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       ptx::mbar_init(b_vfull(s), 1);
       ptx::mbar_init(b_vempty(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      ptx::mbar_init(b_sfull(b), 1);
-      ptx::mbar_init(b_pfull(b), kSoftmaxThreads / 2);
-      ptx::mbar_init(b_odone(b), 1);
+    for (int x = 0; x < 2; ++x) {
+      ptx::mbar_init(b_sfull(x), 1);
+      ptx::mbar_init(b_pfull(x), 128);
+      ptx::mbar_init(b_odone(x), 1);
     }
-    ptx::mbar_init(b_red, kSoftmaxWarps);
     ptx::mbar_init(b_final, 1);
     // A CTA starting after another one failed does no work.
     *abort_flag = *reinterpret_cast<volatile int*>(&g_device_status) != 0 ? 1 : 0;
@@ -286,17 +296,18 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   } else if (warp == kWarpTma) {
     // ================================================================ producer
     if (lane == 0) {
-      ptx::mbar_arrive_expect_tx(b_q, kTileBytes);
-      for (int hf = 0; hf < kHalves; ++hf)
-        ptx::tma_load_3d(s_q + hf * kBoxBytes, &p.tm_q, b_q, hf * 64, head, wk.q_start + q0);
+      ptx::mbar_arrive_expect_tx(b_q, 2 * kTileBytes);
+      for (int x = 0; x < 2; ++x)
+        for (int hf = 0; hf < kHalves; ++hf)
+          ptx::tma_load_3d(s_q + x * kTileBytes + hf * kBoxBytes, &p.tm_q, b_q, hf * 64, head,
+                           wk.q_start + q0 + x * kBlockM);
     }
     int k_issued = 0, v_issued = 0;
     for (int t = 0; t < n_tiles; ++t) {
       const int s = t % kStages;
       const uint32_t ph = (t / kStages) & 1;
-      const int sg = t < tiles0 ? 0 : 1;
-      const int key0 = (sg == 0 ? t : t - tiles0) * kBlockN;
-      const hcp_kv_segment& seg = wk.seg[sg];
+      const int key0 = tile_key0(t);
+      const hcp_kv_segment& seg = wk.seg[tile_seg(t)];
       const uint32_t s_k = s_kv0 + (2 * s) * kTileBytes;
       const uint32_t s_v = s_k + kTileBytes;
       int blk_ids[8];
@@ -361,84 +372,104 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   } else if (warp == kWarpMma) {
     // ================================================================ MMA issuer
     bool ok = __all_sync(0xffffffffu, wait_bar(b_q, 0, abort_flag, kErrWaitMma));
-    auto issue_pv = [&](int j) -> bool {
-      const int s = j % kStages;
-      const uint32_t ph = (j / kStages) & 1;
-      const int b = j & 1;
-      if (!__all_sync(0xffffffffu, wait_bar(b_pfull(b), (j >> 1) & 1, abort_flag, kErrWaitMma)))
-        return false;
-      if (!__all_sync(0xffffffffu, wait_bar(b_vfull(s), ph, abort_flag, kErrWaitMma))) return false;
-      ptx::tc_fence_after();
-      if (lane == 0) {
-        const uint32_t s_v = s_kv0 + (2 * s + 1) * kTileBytes;
-#pragma unroll
-        const uint32_t o_acc = tmem + 256 + b * D;  // O_b accumulates the tiles of parity b
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
-          ptx::umma_ts(o_acc, tmem + b * 128 + kk * 8, bdesc, kIdescPV, (j >= 2 || kk > 0) ? 1u : 0u);
-        }
-        if (precise) {
-#pragma unroll
-          for (int kk = 0; kk < kBlockN / 16; ++kk) {
-            const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
-            ptx::umma_ts(o_acc, tmem + b * 128 + 64 + kk * 8, bdesc, kIdescPV, 1u);
+    int pv_count[2] = {0, 0};  // PV products issued per query tile
+    for (int t = 0; t <= n_tiles && ok; ++t) {
+      const bool have_prev = t >= 1;
+      const bool have_cur = t < n_tiles;
+      const int sp = (t - 1) % kStages;   // stage of tile t-1
+      const int sc = t % kStages;         // stage of tile t
+      bool v_ready = false, k_ready = false;
+      for (int x = 0; x < 2 && ok; ++x) {
+        if (have_prev && active(x, t - 1)) {
+          // O_x += P_x V_{t-1}; P_x is ready once the warpgroup arrived
+          ok = __all_sync(0xffffffffu, wait_bar(b_pfull(x), pv_count[x] & 1, abort_flag, kErrWaitMma));
+          if (ok && !v_ready) {
+            ok = __all_sync(0xffffffffu,
+                            wait_bar(b_vfull(sp), ((t - 1) / kStages) & 1, abort_flag, kErrWaitMma));
+            v_ready = true;
           }
-        }
-        ptx::umma_commit(b_vempty(s));
-        ptx::umma_commit(b_odone(b));
-      }
-      __syncwarp();
-      return true;
-    };
-    for (int t = 0; t < n_tiles && ok; ++t) {
-      const int s = t % kStages;
-      const uint32_t ph = (t / kStages) & 1;
-      const int b = t & 1;
-      ok = __all_sync(0xffffffffu, wait_bar(b_kfull(s), ph, abort_flag, kErrWaitMma));
-      if (!ok) break;
-      ptx::tc_fence_after();
-      if (lane == 0) {
-        const uint32_t s_k = s_kv0 + (2 * s) * kTileBytes;
+          if (!ok) break;
+          ptx::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t s_v = s_kv0 + (2 * sp + 1) * kTileBytes;
+            const uint32_t o_acc = tmem + 256 + x * D;
+            const uint32_t p_col = tmem + x * 128;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-          const uint64_t adesc = ptx::sdesc_sw128(s_q + off, 16, 1024);
-          const uint64_t bdesc = ptx::sdesc_sw128(s_k + off, 16, 1024);
-          ptx::umma_ss(tmem + b * 128, adesc, bdesc, kIdescQK, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kBlockN / 16; ++kk) {
+              const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
+              ptx::umma_ts(o_acc, p_col + kk * 8, bdesc, kIdescPV,
+                           (pv_count[x] > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (x == 0 ? precise_a : precise_b) {
+#pragma unroll
+              for (int kk = 0; kk < kBlockN / 16; ++kk) {
+                const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
+                ptx::umma_ts(o_acc, p_col + 64 + kk * 8, bdesc, kIdescPV, 1u);
+              }
+            }
+            ptx::umma_commit(b_odone(x));
+          }
+          __syncwarp();
+          ++pv_count[x];
         }
-        ptx::umma_commit(b_sfull(b));
-        ptx::umma_commit(b_kempty(s));
+        if (have_cur && active(x, t)) {
+          // S_x = Q_x K_t
+          if (!k_ready) {
+            ok = __all_sync(0xffffffffu,
+                            wait_bar(b_kfull(sc), (t / kStages) & 1, abort_flag, kErrWaitMma));
+            if (!ok) break;
+            k_ready = true;
+          }
+          ptx::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t s_k = s_kv0 + (2 * sc) * kTileBytes;
+            const uint32_t s_qx = s_q + x * kTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+              const uint64_t adesc = ptx::sdesc_sw128(s_qx + off, 16, 1024);
+              const uint64_t bdesc = ptx::sdesc_sw128(s_k + off, 16, 1024);
+              ptx::umma_ss(tmem + x * 128, adesc, bdesc, kIdescQK, kk > 0 ? 1u : 0u);
+            }
+            ptx::umma_commit(b_sfull(x));
+          }
+          __syncwarp();
+        }
+      }
+      if (!ok) break;
+      // release the stages (tcgen05.commit tracks every MMA issued so far)
+      if (lane == 0) {
+        if (have_prev) ptx::umma_commit(b_vempty(sp));
+        if (have_cur) ptx::umma_commit(b_kempty(sc));
       }
       __syncwarp();
-      if (t >= 1) ok = issue_pv(t - 1);
     }
-    if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
     // Teardown: no MMA may be in flight when TMEM is released.
     if (lane == 0) ptx::umma_commit(b_final);
     __syncwarp();
     drain_bar(b_final, 0);
   } else {
     // ================================================================ softmax + epilogue
-    const int g = warp >> 2;                 // warpgroup: KV tiles t with t % 2 == g
+    const int x = warp >> 2;                 // query tile of this warpgroup (0 = A, 1 = B)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;     // == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const int qrow = q0 + row;               // work-item-relative query row
+    const int qrow = q0 + x * kBlockM + row;  // work-item-relative query row
+    const bool precise = x == 0 ? precise_a : precise_b;
     const float scale_log2 = p.scale_log2;
-    const uint32_t s_addr = tmem + lane_base + g * 128;
-    const uint32_t o_own = tmem + lane_base + 256 + g * D;
-    constexpr int kOHalf = D / 2;            // output columns this thread writes
-    float m_used = -INFINITY;  // running max over this warpgroup's tiles, base-2 scaled domain
-    float l = 0.f;             // row sum over this warpgroup's tiles
+    const uint32_t s_addr = tmem + lane_base + x * 128;
+    const uint32_t o_addr = tmem + lane_base + 256 + x * D;
+    float m_used = -INFINITY;  // running max of the row, base-2 scaled domain
+    float l = 0.f;             // row sum
     bool ok = true;
-    int my_tiles = 0;
-    for (int t = g; t < n_tiles; t += 2) {
-      ok = __all_sync(0xffffffffu, wait_bar(b_sfull(g), (t >> 1) & 1, abort_flag, kErrWaitSoftmax));
+    int done = 0;              // KV tiles processed by this warpgroup
+    for (int t = 0; t < n_tiles; ++t) {
+      if (!active(x, t)) continue;
+      ok = __all_sync(0xffffffffu, wait_bar(b_sfull(x), done & 1, abort_flag, kErrWaitSoftmax));
       if (!ok) break;
       ptx::tc_fence_after();
-      const int sg = t < tiles0 ? 0 : 1;
-      const int key0 = (sg == 0 ? t : t - tiles0) * kBlockN;
-      const hcp_kv_segment& seg = wk.seg[sg];
+      const int key0 = tile_key0(t);
+      const hcp_kv_segment& seg = wk.seg[tile_seg(t)];
       int vis = seg.len - key0;
       if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
       vis = max(0, min(vis, kBlockN));
@@ -501,64 +532,39 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       l = l * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
       m_used = m_new;
 
-      if (my_tiles >= 1) {
-        // O_g += P V of this warpgroup's previous tile must have landed before
-        // O_g is rescaled and before this P is released to the MMA warp.
-        ok = __all_sync(0xffffffffu,
-                        wait_bar(b_odone(g), (my_tiles - 1) & 1, abort_flag, kErrWaitSoftmax));
+      if (done >= 1) {
+        // O_x += P V of the previous tile must have landed before O_x is
+        // rescaled and before this P is released to the MMA warp.
+        ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), (done - 1) & 1, abort_flag, kErrWaitSoftmax));
         if (!ok) break;
         ptx::tc_fence_after();
         if (__any_sync(0xffffffffu, raise)) {
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
-            ptx::tmem_ld_32x32b_x32(o_own + c * 32, o);
+            ptx::tmem_ld_32x32b_x32(o_addr + c * 32, o);
             ptx::tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            ptx::tmem_st_32x32b_x32(o_own + c * 32, o);
+            ptx::tmem_st_32x32b_x32(o_addr + c * 32, o);
           }
         }
       }
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(b_pfull(g));
-      ++my_tiles;
+      ptx::mbar_arrive(b_pfull(x));
+      ++done;
     }
-    if (ok && my_tiles > 0) {
-      ok = __all_sync(0xffffffffu,
-                      wait_bar(b_odone(g), (my_tiles - 1) & 1, abort_flag, kErrWaitSoftmax));
-      ptx::tc_fence_after();
-    }
-    // exchange (running max, row sum) with the other warpgroup; its O buffer
-    // is complete once it has arrived here
-    float2* xch = reinterpret_cast<float2*>(red);  // [2][128]
-    if (ok) {
-      xch[g * 128 + row] = make_float2(m_used, l);
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(b_red);
-      ok = __all_sync(0xffffffffu, wait_bar(b_red, 0, abort_flag, kErrWaitSoftmax));
+    if (ok && done > 0) {
+      ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), (done - 1) & 1, abort_flag, kErrWaitSoftmax));
       ptx::tc_fence_after();
     }
     if (ok) {
       // ---------------------------------------------------------- epilogue
-      const float2 other = xch[(g ^ 1) * 128 + row];
-      const float m0 = g == 0 ? m_used : other.x, l0 = g == 0 ? l : other.y;
-      const float m1 = g == 0 ? other.x : m_used, l1 = g == 0 ? other.y : l;
-      const float mm2 = fmaxf(m0, m1);
-      float f0 = 0.f, f1 = 0.f, lsum = 0.f;
-      if (mm2 != -INFINITY) {
-        f0 = l0 > 0.f ? ex2_approx(m0 - mm2) : 0.f;
-        f1 = l1 > 0.f ? ex2_approx(m1 - mm2) : 0.f;
-        lsum = l0 * f0 + l1 * f1;
-      }
       const bool valid = qrow < wk.q_len;
       const float LN2 = 0.69314718055994530942f;
-      float lse_v = (lsum > 0.f) ? (mm2 + lg2_approx(lsum)) * LN2 : -INFINITY;
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      f0 *= inv;
-      f1 *= inv;
+      float lse_v = (l > 0.f) ? (m_used + lg2_approx(l)) * LN2 : -INFINITY;
+      float f_new = (l > 0.f) ? 1.f / l : 0.f;
       float f_old = 0.f;
       const long long out_row = static_cast<long long>(wk.q_start) + qrow;
       const long long lse_idx_col = static_cast<long long>(wk.lse_col) + qrow;
@@ -568,30 +574,28 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
         if (lp == INFINITY) lp = -INFINITY;
         const float mm = fmaxf(lp, lse_v);
         if (mm == -INFINITY) {
-          f0 = f1 = 0.f;
+          f_new = 0.f;
           lse_v = -INFINITY;
         } else {
           const float wp = __expf(lp - mm);
           const float wn = __expf(lse_v - mm);
           const float r = 1.f / (wp + wn);
           f_old = wp * r;
-          f0 *= wn * r;
-          f1 *= wn * r;
+          f_new *= wn * r;
           lse_v = mm + __logf(wp + wn);
         }
       }
-      const bool have0 = n_tiles >= 1, have1 = n_tiles >= 2;
-      const long long col0 = static_cast<long long>(head) * D + g * kOHalf;
+      const long long col0 = static_cast<long long>(head) * D;
 #pragma unroll
-      for (int c = 0; c < kOHalf / 32; ++c) {
-        uint32_t r0[32], r1[32];
-        if (have0) ptx::tmem_ld_32x32b_x32(tmem + lane_base + 256 + g * kOHalf + c * 32, r0);
-        if (have1) ptx::tmem_ld_32x32b_x32(tmem + lane_base + 256 + D + g * kOHalf + c * 32, r1);
-        ptx::tmem_wait_ld();
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        if (done > 0) {
+          ptx::tmem_ld_32x32b_x32(o_addr + c * 32, r);
+          ptx::tmem_wait_ld();
+        }
         float o[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          o[i] = (have0 ? __uint_as_float(r0[i]) * f0 : 0.f) + (have1 ? __uint_as_float(r1[i]) * f1 : 0.f);
+        for (int i = 0; i < 32; ++i) o[i] = done > 0 ? __uint_as_float(r[i]) * f_new : 0.f;
         if (!valid) continue;
         if (merging) {
           const long long base = out_row * p.merge_o_row_stride + col0 + c * 32;
@@ -635,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
                                  pack2<F16>(o[8 * q8 + 6], o[8 * q8 + 7]));
         }
       }
-      if (valid && p.lse != nullptr && g == 0) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
+      if (valid && p.lse != nullptr) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
     }
   }
 
