@@ -160,6 +160,18 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// Per-warpgroup register budget change; every warp of the warpgroup must
+// execute the same instruction.  The sum over the CTA must stay within the
+// registers the CTA was launched with.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------ descriptors
 // SM100 shared-memory matrix descriptor, 128-byte swizzle.
 //   bits  0-13 start address >> 4
