@@ -11,7 +11,7 @@
 // bound by operand traffic (L2 -> shared memory -> tensor core), and sharing
 // halves it per FLOP.
 //
-// Warp roles (384 threads; warps 10-11 only complete the third warpgroup):
+// Warp roles (320 threads):
 //   warps 0-3  softmax / O correction / epilogue of query tile A
 //   warps 4-7  the same for query tile B.  Thread (w, lane) owns row
 //              32*(w%4)+lane of its tile, which is that TMEM lane.
@@ -57,19 +57,12 @@ constexpr int kBlockN = 128;          // keys per KV tile
 constexpr int kStages = 2;
 constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
-constexpr int kThreads = 384;  // 3 warpgroups: softmax A, softmax B, TMA + MMA (+2 idle warps)
-// Register budget after setmaxnreg: 2 x 128 softmax threads at kRegsSoftmax
-// plus 128 producer/MMA threads at kRegsOther must equal the launch budget
-// 384 x 168 (the per-thread cap with three warps per SM sub-partition).
-constexpr int kRegsSoftmax = 224;
-constexpr int kRegsOther = 56;
-static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther == 384 * 168, "register split");
+constexpr int kThreads = 320;
 constexpr int kMaxWork = 160;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
 constexpr float kRescaleThreshold = 8.0f;            // log2 units
 constexpr int kPreciseKeys = 256;  // rows seeing fewer keys get the hi+lo P product
-constexpr int kEmuPairs = 5;       // of every 16 key pairs, exp2 on the FMA pipe (full tiles)
 
 // Failure codes written to g_device_status.
 enum : int {
@@ -155,59 +148,6 @@ __device__ __forceinline__ float lg2_approx(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Packed fp32x2 arithmetic (one instruction for two lanes' worth of FMA).
-__device__ __forceinline__ uint64_t f2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ float2 f2_split(uint64_t v) {
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// 2^x for two lanes on the FMA pipe, x <= 8.  Cody-Waite style reduction
-// x = n + f with n = round(x) (magic-number rounding, |f| <= 1/2), then a
-// degree-3 polynomial for 2^f fitted here by iteratively reweighted least
-// squares on the relative error (max relative error 7.5e-5 in fp32, well
-// below the 2^-9 rounding of the 16-bit P it feeds), and n is added to the
-// exponent field.  Arguments below -120 are clamped (2^-120 ~ 7.5e-37).
-__device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  float2 x = f2_split(x2);
-  x.x = fmaxf(x.x, -120.f);
-  x.y = fmaxf(x.y, -120.f);
-  const uint64_t xc = f2(x.x, x.y);
-  const uint64_t t = fadd2(xc, f2(kMagic, kMagic));        // round(x) in the low mantissa bits
-  const uint64_t r = fadd2(t, f2(-kMagic, -kMagic));       // round(x) as a float
-  const uint64_t f = ffma2(r, f2(-1.f, -1.f), xc);         // x - round(x)
-  uint64_t p = ffma2(f2(0.05517113208770752f, 0.05517113208770752f), f,
-                     f2(0.24261008203029633f, 0.24261008203029633f));
-  p = ffma2(p, f, f2(0.6932609677314758f, 0.6932609677314758f));
-  p = ffma2(p, f, f2(0.9999281167984009f, 0.9999281167984009f));
-  const float2 tt = f2_split(t);
-  const float2 pp = f2_split(p);
-  const float lo = __int_as_float(__float_as_int(pp.x) + (__float_as_int(tt.x) << 23));
-  const float hi = __int_as_float(__float_as_int(pp.y) + (__float_as_int(tt.y) << 23));
-  return f2(lo, hi);
 }
 
 template <bool F16>
@@ -351,11 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   const uint32_t tmem = *tmem_slot;
   const bool skip_all = *abort_flag != 0;
 
-  // Each role branch sets its own register budget (ptxas allocates every
-  // branch under the budget that dominates it).
-  if (warp >= kWarpTma) {
-    ptx::setmaxnreg_dec<kRegsOther>();
-  if (skip_all || warp > kWarpMma) {
+  if (skip_all) {
     // nothing issued, nothing to drain
   } else if (warp == kWarpTma) {
     // ================================================================ producer
@@ -437,14 +373,6 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     // ================================================================ MMA issuer
     bool ok = __all_sync(0xffffffffu, wait_bar(b_q, 0, abort_flag, kErrWaitMma));
     int pv_count[2] = {0, 0};  // PV products issued per query tile
-    // last KV tile each query tile needs (its final PV product signals b_odone)
-    int last_tile[2];
-    {
-      const int need0[2] = {ka0, kb0}, need1[2] = {ka1, kb1};
-      for (int xx = 0; xx < 2; ++xx)
-        last_tile[xx] = need1[xx] > 0 ? tiles0 + (need1[xx] + kBlockN - 1) / kBlockN - 1
-                                      : (need0[xx] + kBlockN - 1) / kBlockN - 1;
-    }
     for (int t = 0; t <= n_tiles && ok; ++t) {
       const bool have_prev = t >= 1;
       const bool have_cur = t < n_tiles;
@@ -479,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
                 ptx::umma_ts(o_acc, p_col + 64 + kk * 8, bdesc, kIdescPV, 1u);
               }
             }
-            if (t - 1 == last_tile[x]) ptx::umma_commit(b_odone(x));
+            ptx::umma_commit(b_odone(x));
           }
           __syncwarp();
           ++pv_count[x];
@@ -520,10 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     if (lane == 0) ptx::umma_commit(b_final);
     __syncwarp();
     drain_bar(b_final, 0);
-  }
   } else {
-    ptx::setmaxnreg_inc<kRegsSoftmax>();
-  if (!skip_all) {
     // ================================================================ softmax + epilogue
     const int x = warp >> 2;                 // query tile of this warpgroup (0 = A, 1 = B)
     const int quarter = warp & 3;
@@ -538,83 +463,51 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     float l = 0.f;             // row sum
     bool ok = true;
     int done = 0;              // KV tiles processed by this warpgroup
-    const uint64_t scale2 = f2(scale_log2, scale_log2);
     for (int t = 0; t < n_tiles; ++t) {
       if (!active(x, t)) continue;
-      // S_x is ready; the commit behind this barrier also covers every earlier
-      // MMA, so O_x += P V of the previous tile has landed too.
       ok = __all_sync(0xffffffffu, wait_bar(b_sfull(x), done & 1, abort_flag, kErrWaitSoftmax));
       if (!ok) break;
       ptx::tc_fence_after();
-      uint32_t sr[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        ptx::tmem_ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       const int key0 = tile_key0(t);
       const hcp_kv_segment& seg = wk.seg[tile_seg(t)];
       int vis = seg.len - key0;
       if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
       vis = max(0, min(vis, kBlockN));
-      const bool full = __all_sync(0xffffffffu, vis >= kBlockN);
+
+      uint32_t sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        ptx::tmem_ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       ptx::tmem_wait_ld();
-      if (!full) {
+      if (vis < kBlockN) {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
           if (i >= vis) sr[i] = __float_as_uint(-INFINITY);
       }
       float mx8[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        mx8[j] = fmax3(__uint_as_float(sr[j]), __uint_as_float(sr[j + 8]), __uint_as_float(sr[j + 16]));
+      for (int j = 0; j < 8; ++j) mx8[j] = __uint_as_float(sr[j]);
 #pragma unroll
-      for (int i = 24; i < 120; i += 16) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          mx8[j] = fmax3(mx8[j], __uint_as_float(sr[i + j]), __uint_as_float(sr[i + 8 + j]));
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(mx8[j], __uint_as_float(sr[120 + j]));
-      const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
-                             fmaxf(mx8[6], mx8[7]));
+      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mx2 = mx * scale_log2;  // -inf stays -inf
       const bool raise = mx2 > m_used + kRescaleThreshold;
       const float m_new = raise ? mx2 : m_used;
       const float alpha = raise ? ex2_approx(m_used - m_new) : 1.f;  // 0 when m_used = -inf
       const float m_base = (m_new == -INFINITY) ? 0.f : m_new;
-      // O_x is stable here (its next PV waits for this warpgroup): rescale it
-      // when the running max moved.
-      if (done >= 1 && __any_sync(0xffffffffu, raise)) {
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          ptx::tmem_ld_32x32b_x32(o_addr + c * 32, o);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          ptx::tmem_st_32x32b_x32(o_addr + c * 32, o);
-        }
-      }
-      const uint64_t negm2 = f2(-m_base, -m_base);
-      uint64_t sum2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+      float sums[4] = {0.f, 0.f, 0.f, 0.f};
       if (!precise) {
-        const bool emulate = full;  // emulated exp2 only where no key is masked
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const uint64_t xx = ffma2(f2(__uint_as_float(sr[c * 32 + 2 * i]),
-                                         __uint_as_float(sr[c * 32 + 2 * i + 1])), scale2, negm2);
-            uint64_t pp;
-            if (i < kEmuPairs && emulate) {
-              pp = exp2_fma2(xx);
-            } else {
-              const float2 xf = f2_split(xx);
-              pp = f2(ex2_approx(xf.x), ex2_approx(xf.y));
-            }
-            sum2[i & 1] = fadd2(sum2[i & 1], pp);
-            const float2 pf = f2_split(pp);
-            pk[i] = pack2<F16>(pf.x, pf.y);
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
+            const float p1 =
+                ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+            sums[i & 3] += p0 + p1;
+            pk[i] = pack2<F16>(p0, p1);
           }
           ptx::tmem_st_32x32b_x16(s_addr + c * 16, pk);
         }
@@ -624,11 +517,10 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
           uint32_t pk[16], pl[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const uint64_t xx = ffma2(f2(__uint_as_float(sr[c * 32 + 2 * i]),
-                                         __uint_as_float(sr[c * 32 + 2 * i + 1])), scale2, negm2);
-            const float2 xf = f2_split(xx);
-            const float p0 = ex2_approx(xf.x), p1 = ex2_approx(xf.y);
-            sum2[i & 1] = fadd2(sum2[i & 1], f2(p0, p1));
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
+            const float p1 =
+                ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+            sums[i & 3] += p0 + p1;
             pk[i] = pack2<F16>(p0, p1);
             const float2 h2 = unpack2<F16>(pk[i]);
             pl[i] = pack2<F16>(p0 - h2.x, p1 - h2.y);
@@ -637,17 +529,34 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
           ptx::tmem_st_32x32b_x16(s_addr + 64 + c * 16, pl);
         }
       }
-      const float2 sa = f2_split(fadd2(sum2[0], sum2[1]));
-      l = l * alpha + (sa.x + sa.y);
+      l = l * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
       m_used = m_new;
+
+      if (done >= 1) {
+        // O_x += P V of the previous tile must have landed before O_x is
+        // rescaled and before this P is released to the MMA warp.
+        ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), (done - 1) & 1, abort_flag, kErrWaitSoftmax));
+        if (!ok) break;
+        ptx::tc_fence_after();
+        if (__any_sync(0xffffffffu, raise)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            ptx::tmem_ld_32x32b_x32(o_addr + c * 32, o);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            ptx::tmem_st_32x32b_x32(o_addr + c * 32, o);
+          }
+        }
+      }
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       ptx::mbar_arrive(b_pfull(x));
       ++done;
     }
     if (ok && done > 0) {
-      // the MMA warp commits this barrier once, after O_x's last PV product
-      ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), 0, abort_flag, kErrWaitSoftmax));
+      ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), (done - 1) & 1, abort_flag, kErrWaitSoftmax));
       ptx::tc_fence_after();
     }
     if (ok) {
@@ -732,7 +641,6 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       }
       if (valid && p.lse != nullptr) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
     }
-  }
   }
 
   // ---- teardown: release TMEM once every role is done with it
