@@ -72,6 +72,41 @@ class HcpFwdArgs(ctypes.Structure):
     ]
 
 
+class HcpDecodeSeq(ctypes.Structure):
+    _fields_ = [
+        ("q_row", ctypes.c_int32),
+        ("peer_start", ctypes.c_int32),
+        ("peer_len", ctypes.c_int32),
+        ("paged_req", ctypes.c_int32),
+        ("local_start", ctypes.c_int32),
+        ("local_len", ctypes.c_int32),
+    ]
+
+
+class HcpDecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("chunk_keys", ctypes.c_int32),
+        ("q", ctypes.c_void_p), ("q_rows", ctypes.c_int64), ("q_row_stride", ctypes.c_int64),
+        ("peer_k", ctypes.c_void_p), ("peer_v", ctypes.c_void_p), ("peer_rows", ctypes.c_int64),
+        ("peer_row_stride", ctypes.c_int64),
+        ("kv_cache", ctypes.c_void_p), ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int32), ("_pad0", ctypes.c_int32),
+        ("block_table", ctypes.c_void_p), ("block_table_stride", ctypes.c_int64),
+        ("block_table_rows", ctypes.c_int64),
+        ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int32), ("_pad1", ctypes.c_int32),
+        ("out_row_stride", ctypes.c_int64),
+        ("lse", ctypes.c_void_p), ("lse_stride", ctypes.c_int64),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
+        ("seqs", ctypes.POINTER(HcpDecodeSeq)), ("num_seqs", ctypes.c_int32),
+        ("_pad2", ctypes.c_int32),
+    ]
+
+
 # Every C entry point with its ctypes signature.  ``tests`` check that the
 # built library exports exactly the names ``include/hcp_ring.h`` declares.
 SIGNATURES = {
@@ -82,6 +117,12 @@ SIGNATURES = {
         ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
         ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
+    "hcp_ring_decode_splitkv": (ctypes.c_int, [ctypes.POINTER(HcpDecodeArgs), ctypes.c_void_p]),
+    "hcp_decode_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(HcpDecodeArgs)]),
+    "hcp_kv_cache_update": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     "hcp_get_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "hcp_reset_device_status": (ctypes.c_int, []),
     "hcp_version": (ctypes.c_char_p, []),

@@ -16,8 +16,10 @@
 #include <vector>
 
 #include "hcp_ring.h"
-#include "merge.cuh"
 #include "ring_fwd.cuh"
+#include "decode.cuh"
+#include "cache.cuh"
+#include "merge.cuh"
 
 namespace hcp {
 namespace {
@@ -77,6 +79,7 @@ bool encode_rows_heads(CUtensorMap* m, bool f16, const void* base, int64_t rows,
 
 std::mutex g_attr_mu;
 bool g_attr_done[2][2][64];
+bool g_dec_attr_done[2][2][64];
 
 template <int D, bool F16>
 int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
@@ -128,6 +131,51 @@ int validate_segment(const hcp_fwd_args* a, const hcp_attn_work& w, const hcp_kv
     default:
       return HCP_ERR_INVALID;
   }
+}
+
+template <int D, bool F16>
+int launch_decode(const DecodeParams& p, int units, int hkv, cudaStream_t st) {
+  constexpr int smem = DecSmem<D>::kBytes;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    bool& done = g_dec_attr_done[D == 128][F16][dev];
+    if (!done) {
+      if (cudaFuncSetAttribute(decode_splitkv_kernel<D, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return HCP_ERR_CUDA;
+      done = true;
+    }
+  }
+  decode_splitkv_kernel<D, F16><<<dim3(units, hkv), kDecThreads, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
+// Keys per split-KV chunk: enough chunks for ~4 waves of 2 CTAs per SM.
+int decode_chunk_keys(const hcp_decode_args* a) {
+  if (a->chunk_keys > 0) return ((a->chunk_keys + kDecTileKeys - 1) / kDecTileKeys) * kDecTileKeys;
+  int64_t total = 0;
+  for (int i = 0; i < a->num_seqs; ++i) total += a->seqs[i].peer_len + a->seqs[i].local_len;
+  const int64_t want_units = std::max<int64_t>(1, (8 * 148) / std::max(1, a->num_kv_heads));
+  int64_t c = (total + want_units - 1) / want_units;
+  c = ((c + kDecTileKeys - 1) / kDecTileKeys) * kDecTileKeys;
+  return static_cast<int>(std::min<int64_t>(8192, std::max<int64_t>(256, c)));
+}
+
+int64_t decode_units(const hcp_decode_args* a, int chunk) {
+  int64_t u = 0;
+  for (int i = 0; i < a->num_seqs; ++i) {
+    const int64_t pu = (a->seqs[i].peer_len + chunk - 1) / chunk;
+    const int64_t lu = (a->seqs[i].local_len + chunk - 1) / chunk;
+    u += std::max<int64_t>(1, pu + lu);
+  }
+  return u;
+}
+
+int64_t workspace_need(const hcp_decode_args* a, int chunk) {
+  const int64_t units = decode_units(a, chunk);
+  return units * a->num_heads * (static_cast<int64_t>(a->head_dim) + 1) * 4;
 }
 
 }  // namespace
@@ -328,3 +376,173 @@ extern "C" int hcp_reset_device_status(void) {
 }
 
 extern "C" const char* hcp_version(void) { return "hcp_ring 0.1.0 (sm_100a)"; }
+
+namespace {
+int validate_decode(const hcp_decode_args* a) {
+  if (a == nullptr) return HCP_ERR_INVALID;
+  if (a->dtype != HCP_BF16 && a->dtype != HCP_F16) return HCP_ERR_UNSUPPORTED;
+  const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim;
+  if (H <= 0 || Hkv <= 0 || H % Hkv != 0 || H / Hkv > kDecMaxGroup) return HCP_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128) return HCP_ERR_UNSUPPORTED;
+  if (!(a->scale > 0.f) || !std::isfinite(a->scale)) return HCP_ERR_INVALID;
+  if (a->num_seqs < 0 || (a->num_seqs > 0 && a->seqs == nullptr)) return HCP_ERR_INVALID;
+  if (a->q == nullptr || a->out == nullptr || a->q_row_stride < static_cast<int64_t>(H) * D ||
+      a->out_row_stride < static_cast<int64_t>(H) * D || (a->q_row_stride % 8) != 0 || !aligned16(a->q))
+    return HCP_ERR_INVALID;
+  if (a->out_dtype != a->dtype && a->out_dtype != HCP_F32) return HCP_ERR_UNSUPPORTED;
+  const bool peer = a->peer_k != nullptr, paged = a->kv_cache != nullptr;
+  const int64_t kv_row = static_cast<int64_t>(Hkv) * D;
+  if (peer && (a->peer_v == nullptr || a->peer_rows <= 0 || a->peer_row_stride < kv_row ||
+               (a->peer_row_stride % 8) != 0 || !aligned16(a->peer_k) || !aligned16(a->peer_v)))
+    return HCP_ERR_INVALID;
+  if (paged) {
+    const int bs = a->block_size;
+    if (bs != 16 && bs != 32 && bs != 64) return HCP_ERR_UNSUPPORTED;
+    if (a->num_blocks <= 0 || a->num_blocks >= (1ll << 31) || a->block_table == nullptr ||
+        a->block_table_stride <= 0 || a->block_table_rows <= 0 || !aligned16(a->kv_cache))
+      return HCP_ERR_INVALID;
+  }
+  for (int i = 0; i < a->num_seqs; ++i) {
+    const hcp_decode_seq& q = a->seqs[i];
+    if (q.q_row < 0 || q.q_row >= a->q_rows || q.peer_len < 0 || q.local_len < 0 || q.peer_start < 0)
+      return HCP_ERR_INVALID;
+    if (q.peer_len > 0 && (!peer || static_cast<int64_t>(q.peer_start) + q.peer_len > a->peer_rows))
+      return HCP_ERR_INVALID;
+    if (q.local_len > 0) {
+      if (!paged || q.paged_req < 0 || q.paged_req >= a->block_table_rows || q.local_start < 0)
+        return HCP_ERR_INVALID;
+      if (q.local_start % a->block_size != 0) return HCP_ERR_UNSUPPORTED;
+      if (static_cast<int64_t>(q.local_start) + q.local_len > a->block_table_stride * a->block_size)
+        return HCP_ERR_INVALID;
+    }
+    if (a->lse != nullptr && q.q_row >= a->lse_stride) return HCP_ERR_INVALID;
+  }
+  return HCP_OK;
+}
+}  // namespace
+
+extern "C" int64_t hcp_decode_workspace_bytes(const hcp_decode_args* a) {
+  if (validate_decode(a) != HCP_OK) return -1;
+  return workspace_need(a, decode_chunk_keys(a));
+}
+
+extern "C" int hcp_ring_decode_splitkv(const hcp_decode_args* a, void* stream) {
+  const int rc0 = validate_decode(a);
+  if (rc0 != HCP_OK) return rc0;
+  if (a->num_seqs == 0) return HCP_OK;
+  const bool f16 = a->dtype == HCP_F16;
+  const int H = a->num_heads, Hkv = a->num_kv_heads, D = a->head_dim;
+  const int chunk = decode_chunk_keys(a);
+  const int64_t need = workspace_need(a, chunk);
+  if (a->workspace == nullptr || a->workspace_bytes < need || !aligned16(a->workspace))
+    return HCP_ERR_INVALID;
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  // placeholder maps: a tiny valid map over q stands in for an absent source
+  if (!encode_rows_heads(&p.tm_pk, f16, a->q, a->q_rows, H, D, a->q_row_stride)) return HCP_ERR_CUDA;
+  p.tm_pv = p.tm_cache = p.tm_pk;
+  if (a->peer_k != nullptr) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Hkv), static_cast<uint64_t>(a->peer_rows)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(a->peer_row_stride) * 2};
+    const uint32_t box[3] = {64, 1, kDecTileKeys};
+    if (!encode_map(&p.tm_pk, f16, 3, a->peer_k, dims, strides, box) ||
+        !encode_map(&p.tm_pv, f16, 3, a->peer_v, dims, strides, box))
+      return HCP_ERR_CUDA;
+  }
+  if (a->kv_cache != nullptr) {
+    const uint64_t bs = static_cast<uint64_t>(a->block_size);
+    const uint64_t dims[4] = {static_cast<uint64_t>(2 * D), bs, static_cast<uint64_t>(Hkv),
+                              static_cast<uint64_t>(a->num_blocks)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(2 * D) * 2, bs * 2 * D * 2,
+                                 static_cast<uint64_t>(Hkv) * bs * 2 * D * 2};
+    const uint32_t box[4] = {64, static_cast<uint32_t>(bs), 1, 1};
+    if (!encode_map(&p.tm_cache, f16, 4, a->kv_cache, dims, strides, box)) return HCP_ERR_CUDA;
+  }
+  p.q = a->q;
+  p.q_row_stride = a->q_row_stride;
+  p.block_table = a->block_table;
+  p.bt_stride = a->block_table_stride;
+  p.bt_rows = a->block_table_rows;
+  p.num_blocks = a->num_blocks;
+  p.num_heads = H;
+  p.num_kv_heads = Hkv;
+  p.group = H / Hkv;
+  p.block_size = a->kv_cache != nullptr ? a->block_size : 16;
+  p.chunk_keys = chunk;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  float* part_o = static_cast<float*>(a->workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t unit_base = 0;
+  for (int base = 0; base < a->num_seqs; base += kDecMaxSeqs) {
+    const int n = std::min(kDecMaxSeqs, a->num_seqs - base);
+    int units = 0;
+    CombineParams c;
+    std::memset(&c, 0, sizeof(c));
+    for (int i = 0; i < n; ++i) {
+      const hcp_decode_seq& q = a->seqs[base + i];
+      p.seq[i] = DecodeSeq{q.q_row, q.peer_start, q.peer_len, q.paged_req, q.local_start, q.local_len};
+      p.unit_off[i] = units;
+      c.unit_off[i] = units;
+      c.q_row[i] = q.q_row;
+      const int pu = (q.peer_len + chunk - 1) / chunk, lu = (q.local_len + chunk - 1) / chunk;
+      units += std::max(1, pu + lu);  // an empty sequence still gets one (empty) unit
+    }
+    p.unit_off[n] = c.unit_off[n] = units;
+    p.num_seqs = n;
+    p.total_units = units;
+    p.part_o = part_o + unit_base * H * D;
+    const int64_t total_units = decode_units(a, chunk);
+    p.part_lse = part_o + total_units * H * D + unit_base * H;
+    int rc = D == 128 ? (f16 ? launch_decode<128, true>(p, units, Hkv, st) : launch_decode<128, false>(p, units, Hkv, st))
+                      : (f16 ? launch_decode<64, true>(p, units, Hkv, st) : launch_decode<64, false>(p, units, Hkv, st));
+    if (rc != HCP_OK) return rc;
+    c.part_o = p.part_o;
+    c.part_lse = p.part_lse;
+    c.out = a->out;
+    c.out_row_stride = a->out_row_stride;
+    c.lse = a->lse;
+    c.lse_stride = a->lse_stride;
+    c.out_dt = a->out_dtype;
+    c.num_heads = H;
+    c.head_dim = D;
+    c.num_seqs = n;
+    decode_combine_kernel<<<dim3(n, H), 128, 0, st>>>(c);
+    if (cudaGetLastError() != cudaSuccess) return HCP_ERR_CUDA;
+    unit_base += units;
+  }
+  return HCP_OK;
+}
+
+extern "C" int hcp_kv_cache_update(const void* key, const void* value, int64_t num_tokens,
+                                   int64_t key_row_stride, int64_t value_row_stride,
+                                   const int64_t* slot_mapping, void* kv_cache, int64_t num_blocks,
+                                   int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                                   int32_t dtype, void* stream) {
+  if (dtype != HCP_BF16 && dtype != HCP_F16) return HCP_ERR_UNSUPPORTED;
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || (head_dim % 8) != 0 || block_size <= 0 ||
+      num_blocks <= 0)
+    return HCP_ERR_INVALID;
+  if (num_tokens == 0) return HCP_OK;
+  const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if (key == nullptr || value == nullptr || slot_mapping == nullptr || kv_cache == nullptr ||
+      key_row_stride < row || value_row_stride < row || (key_row_stride % 8) != 0 ||
+      (value_row_stride % 8) != 0 || !aligned16(key) || !aligned16(value) || !aligned16(kv_cache))
+    return HCP_ERR_INVALID;
+  CacheUpdateParams p;
+  p.key = static_cast<const uint16_t*>(key);
+  p.value = static_cast<const uint16_t*>(value);
+  p.key_row_stride = key_row_stride;
+  p.value_row_stride = value_row_stride;
+  p.slot_mapping = slot_mapping;
+  p.cache = static_cast<uint16_t*>(kv_cache);
+  p.num_blocks = num_blocks;
+  p.num_tokens = num_tokens;
+  p.block_size = block_size;
+  p.num_kv_heads = num_kv_heads;
+  p.head_dim = head_dim;
+  const int64_t warps = num_tokens * num_kv_heads;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
+  kv_cache_update_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}

@@ -195,3 +195,95 @@ def merge_attn_states(
         _ptr(suffix_lse), suffix_lse.stride(0),
         num_tokens, num_heads, head_dim, _stream(output))
     C.check(rc, "hcp_merge_attn_states")
+
+
+DECODE_FIELDS = 6  # q_row, peer_start, peer_len, paged_req, local_start, local_len
+
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Cached device scratch (grown on demand) for the split-KV partials."""
+    key = (device.type, device.index)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
+def decode_args(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, peer_v=None,
+                kv_cache=None, block_table=None, chunk_keys=0):
+    """Build ``hcp_decode_args`` (without workspace) plus the packed sequence array."""
+    if not q.is_cuda or q.dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("q must be a bf16/fp16 CUDA tensor (no CPU path)")
+    seqs = np.ascontiguousarray(seqs, dtype=np.int32).reshape(-1, DECODE_FIELDS)
+    a = C.HcpDecodeArgs()
+    a.dtype = _DT[q.dtype]
+    a.num_heads, a.head_dim = q.shape[1], q.shape[2]
+    a.num_kv_heads = num_kv_heads
+    a.scale = float(scale)
+    a.chunk_keys = int(chunk_keys)
+    a.q, a.q_rows, a.q_row_stride = _ptr(q), q.shape[0], _rows_heads(q, "q")
+    if peer_k is not None:
+        if peer_v is None or peer_k.shape != peer_v.shape or peer_k.dtype != q.dtype:
+            raise ValueError("peer_k/peer_v must match")
+        a.peer_k, a.peer_v = _ptr(peer_k), _ptr(peer_v)
+        a.peer_rows, a.peer_row_stride = peer_k.shape[0], _rows_heads(peer_k, "peer_k")
+    if kv_cache is not None:
+        if kv_cache.dim() != 4 or not kv_cache.is_contiguous() or kv_cache.dtype != q.dtype:
+            raise ValueError("kv_cache must be a contiguous [num_blocks, Hkv, block_size, 2*D] tensor")
+        if block_table is None or block_table.dtype != torch.int32 or block_table.stride(1) != 1:
+            raise ValueError("block_table must be int32 with contiguous rows")
+        a.kv_cache, a.num_blocks, a.block_size = _ptr(kv_cache), kv_cache.shape[0], kv_cache.shape[2]
+        a.block_table = _ptr(block_table)
+        a.block_table_stride, a.block_table_rows = block_table.stride(0), block_table.shape[0]
+    if out.shape[0] < q.shape[0] or out.shape[1:] != q.shape[1:]:
+        raise ValueError("out must be [>= q rows, H, D]")
+    a.out, a.out_dtype, a.out_row_stride = _ptr(out), _DT[out.dtype], _rows_heads(out, "out")
+    if lse is not None:
+        if lse.dtype != torch.float32 or lse.stride(1) != 1 or lse.shape[0] != q.shape[1]:
+            raise ValueError("lse must be float32 [H, cols]")
+        a.lse, a.lse_stride = _ptr(lse), lse.stride(0)
+    a.seqs = seqs.ctypes.data_as(ctypes.POINTER(C.HcpDecodeSeq))
+    a.num_seqs = seqs.shape[0]
+    return a, seqs
+
+
+def decode_splitkv(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, peer_v=None,
+                   kv_cache=None, block_table=None, chunk_keys=0, workspace=None):
+    """Batch-merged split-KV decode (``hcp_ring_decode_splitkv``).
+
+    ``seqs`` rows: (q_row, peer_start, peer_len, paged_req, local_start,
+    local_len).  Every listed key is visible to the sequence's single query.
+    """
+    a, keep = decode_args(q, seqs, scale=scale, num_kv_heads=num_kv_heads, out=out, lse=lse,
+                          peer_k=peer_k, peer_v=peer_v, kv_cache=kv_cache,
+                          block_table=block_table, chunk_keys=chunk_keys)
+    lib = C.load()
+    need = lib.hcp_decode_workspace_bytes(ctypes.byref(a))
+    if need < 0:
+        raise C.HcpError("hcp_decode_workspace_bytes: invalid arguments")
+    ws = workspace if workspace is not None else _workspace(q.device, need)
+    a.workspace, a.workspace_bytes = _ptr(ws), ws.numel() * ws.element_size()
+    C.check(lib.hcp_ring_decode_splitkv(ctypes.byref(a), _stream(q)), "hcp_ring_decode_splitkv")
+    del keep
+
+
+def kv_cache_update(key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tensor,
+                    slot_mapping: torch.Tensor) -> None:
+    """Paged scatter of new K/V rows (``hcp_kv_cache_update``).
+
+    key/value [n, Hkv, D]; kv_cache [num_blocks, Hkv, block_size, 2*D];
+    slot_mapping [n] int64 (negative = padding).
+    """
+    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be a contiguous int64 tensor")
+    if kv_cache.dim() != 4 or not kv_cache.is_contiguous() or kv_cache.dtype != key.dtype:
+        raise ValueError("kv_cache must be a contiguous [num_blocks, Hkv, block_size, 2*D] tensor")
+    n = min(slot_mapping.shape[0], key.shape[0])
+    rc = C.load().hcp_kv_cache_update(
+        _ptr(key), _ptr(value), n, _rows_heads(key, "key"), _rows_heads(value, "value"),
+        _ptr(slot_mapping), _ptr(kv_cache), kv_cache.shape[0], kv_cache.shape[2], key.shape[1],
+        key.shape[2], _DT[key.dtype], _stream(key))
+    C.check(rc, "hcp_kv_cache_update")

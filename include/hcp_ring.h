@@ -128,6 +128,73 @@ int hcp_merge_attn_states(void* out, int32_t out_dtype, int64_t out_row_stride,
                           const float* suffix_lse, int64_t suffix_lse_stride,
                           int64_t num_tokens, int32_t num_heads, int32_t head_dim, void* stream);
 
+/* One decode sequence: a single query token (row q_row of q/out) attends the
+ * peer keys [peer_start, peer_start+peer_len) of peer_k/peer_v (contiguous)
+ * and the local keys [local_start, local_start+local_len) of its paged
+ * sequence (block_table row paged_req; local_start a multiple of block_size),
+ * all visible (a single query: truncate local_len to causal_offset+1). */
+typedef struct hcp_decode_seq {
+  int32_t q_row;
+  int32_t peer_start;
+  int32_t peer_len;
+  int32_t paged_req;
+  int32_t local_start;
+  int32_t local_len;
+} hcp_decode_seq;
+
+typedef struct hcp_decode_args {
+  int32_t dtype;          /* HCP_BF16 or HCP_F16 */
+  int32_t num_heads;      /* H */
+  int32_t num_kv_heads;   /* Hkv; H / Hkv <= 16 */
+  int32_t head_dim;       /* 64 or 128 */
+  float scale;
+  int32_t chunk_keys;     /* keys per split-KV chunk; 0 = chosen by the library */
+  const void* q;          int64_t q_rows; int64_t q_row_stride;
+  const void* peer_k;     const void* peer_v; int64_t peer_rows; int64_t peer_row_stride;
+  const void* kv_cache;   int64_t num_blocks; int32_t block_size; int32_t _pad0;
+  const int32_t* block_table; int64_t block_table_stride; int64_t block_table_rows;
+  void* out;              int32_t out_dtype; int32_t _pad1; int64_t out_row_stride;
+  float* lse;             int64_t lse_stride;        /* [H, lse_stride], may be NULL */
+  void* workspace;        int64_t workspace_bytes;   /* device scratch, 16-byte aligned */
+  const hcp_decode_seq* seqs;  /* HOST array */
+  int32_t num_seqs;
+  int32_t _pad2;
+} hcp_decode_args;
+
+/*
+ * Split-KV decode over a paged local segment plus a contiguous peer segment,
+ * batch-merged (all sequences in one launch), LSE-merged across chunks.
+ * Needs hcp_decode_workspace_bytes(args) bytes of device workspace.
+ *
+ * Replaces, in the reference: the decode-time use of ring_attn_with_lse over
+ * the local segment and the peer chunks plus the LSE merge of the partials
+ * (hcp_vllm_plugin/ring_backend.py:638-727 local partial,
+ * hcp_vllm_plugin/ring_decode.py:187-259 peer partials and _merge_pair
+ * :46-61), and the per-request decode passes of HcpRingAttentionImpl.forward
+ * (ring_backend.py:611-832 with tq == 1).
+ */
+int hcp_ring_decode_splitkv(const hcp_decode_args* args, void* stream);
+
+/* Workspace bytes hcp_ring_decode_splitkv needs for these arguments
+ * (-1 when the arguments are invalid).  No counterpart in the reference. */
+int64_t hcp_decode_workspace_bytes(const hcp_decode_args* args);
+
+/*
+ * Scatter new K/V rows into the paged cache [num_blocks, Hkv, block_size, 2*D]
+ * at slot_mapping (int64, device; slot < 0 = padding, skipped).
+ * key/value: [num_tokens, Hkv, D] with the given row strides (elements).
+ *
+ * Replaces: HcpRingAttentionImpl.do_kv_cache_update
+ * (hcp_vllm_plugin/ring_backend.py:501-539, torch advanced-index scatter
+ * :532-537) in the [num_blocks, Hkv, block_size, 2*D] layout of
+ * hcp_vllm_plugin/file_connector.py:175-179.
+ */
+int hcp_kv_cache_update(const void* key, const void* value, int64_t num_tokens,
+                        int64_t key_row_stride, int64_t value_row_stride,
+                        const int64_t* slot_mapping, void* kv_cache, int64_t num_blocks,
+                        int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                        int32_t dtype, void* stream);
+
 /*
  * Device-side status word shared by all kernels of the library on the
  * current device: 0 when no kernel reported a failure, else the first

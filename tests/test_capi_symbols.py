@@ -15,7 +15,7 @@ def _declared():
         if fn.endswith(".h"):
             src = open(os.path.join(ROOT, "include", fn)).read()
             src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-            names |= set(re.findall(r"^\s*(?:int|const char\*|void)\s+(hcp_\w+)\s*\(", src, flags=re.M))
+            names |= set(re.findall(r"^\s*(?:int64_t|int|const char\*|void)\s+(hcp_\w+)\s*\(", src, flags=re.M))
     return names
 
 
