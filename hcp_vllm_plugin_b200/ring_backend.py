@@ -1,0 +1,278 @@
+"""HCP ring-attention backend for vLLM, B200 (sm_100a) kernels.
+
+Drop-in for the reference's ``hcp_vllm_plugin.ring_backend``: same backend
+name (``CUSTOM``), same impl constructor and ``forward`` contract, same
+peer-KV staging registry that the KV connector fills.  What changes is the
+body of ``forward``:
+
+* reference (``ring_backend.py:576-834``): a Python loop over requests; per
+  request a gather of all paged keys into a contiguous copy, a local causal
+  pass, a peer non-causal pass and an LSE merge - three kernel launches plus
+  copies per request per layer;
+* here: one host sync per engine step (query_start_loc, seq_lens and the
+  first block ids, cached on the metadata object), a host plan
+  (``ring_plan.plan_layer``), then ONE fused prefill launch for every
+  multi-token request (local keys read straight from the paged cache, peer
+  keys from the staged segment, both in one online softmax) and ONE
+  batch-merged split-KV decode launch for every single-token request.
+
+KV cache layout: ``[num_blocks, Hkv, block_size, 2 * head_size]`` with K in
+the first ``head_size`` lanes of the last dimension and V in the second (the
+layout of ``hcp_vllm_plugin/file_connector.py:14-16``).  There is no CPU
+path: every op runs in ``libhcp_ring.so`` and raises if it is missing.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+from vllm.logger import init_logger
+from vllm.v1.attention.backend import AttentionImpl, AttentionType
+from vllm.v1.attention.backends.flash_attn import (
+    FlashAttentionBackend,
+    FlashAttentionMetadataBuilder,
+)
+
+from . import ops
+from .ring_plan import misaligned_paged_starts, plan_layer
+
+logger = init_logger(__name__)
+
+# ---------------------------------------------------------------------------
+# Peer KV staging (module level), same contract as the reference
+# (ring_backend.py:92-136): the connector writes, forward() reads.
+# Keyed by (chunk_key, layer_name); a request is bound to its ORDERED prefix
+# chunk keys by its first block-table block id.
+# ---------------------------------------------------------------------------
+PEER_KV_STAGING: dict[tuple[str, str], tuple[torch.Tensor, torch.Tensor]] = {}
+PEER_REQ_MAP: dict[int, list[str]] = {}
+
+STAGING_STATS: dict = {"max_concurrent_chunks": 0, "max_staged_layers": 0, "last_chunk_len": 0}
+BATCH_STATS: dict = {"max_reqs": 0}
+# Which device paths ran (validation evidence, as the reference's IMPL_STATS).
+IMPL_STATS: dict = {"attn_cuda": 0, "decode_cuda": 0, "cache_update_cuda": 0, "peer_concat": 0}
+
+
+def stage_peer_kv(chunk_key: str, layer_name: str, k: torch.Tensor, v: torch.Tensor) -> None:
+    """Stage one peer chunk's K/V ([T, Hkv, D], K post-RoPE) for one layer."""
+    PEER_KV_STAGING[(chunk_key, layer_name)] = (k, v)
+    STAGING_STATS["max_staged_layers"] = max(STAGING_STATS["max_staged_layers"], len(PEER_KV_STAGING))
+    chunks = {key[0] for key in PEER_KV_STAGING}
+    STAGING_STATS["max_concurrent_chunks"] = max(STAGING_STATS["max_concurrent_chunks"], len(chunks))
+    STAGING_STATS["last_chunk_len"] = int(k.shape[0])
+
+
+def drop_chunk_kv(chunk_key: str) -> int:
+    keys = [key for key in PEER_KV_STAGING if key[0] == chunk_key]
+    for key in keys:
+        del PEER_KV_STAGING[key]
+    return len(keys)
+
+
+def map_request_peer(first_block_id: int, chunk_keys) -> None:
+    if isinstance(chunk_keys, str):
+        chunk_keys = [chunk_keys]
+    PEER_REQ_MAP[first_block_id] = list(chunk_keys)
+
+
+def unmap_request_peer(first_block_id: int) -> None:
+    PEER_REQ_MAP.pop(first_block_id, None)
+
+
+def request_peer_chunk(first_block_id: int) -> list[str] | None:
+    return PEER_REQ_MAP.get(first_block_id)
+
+
+def clear_peer_kv() -> None:
+    PEER_KV_STAGING.clear()
+    PEER_REQ_MAP.clear()
+
+
+def reset_staging_stats() -> None:
+    STAGING_STATS.update(max_concurrent_chunks=0, max_staged_layers=0, last_chunk_len=0)
+
+
+def reset_batch_stats() -> None:
+    BATCH_STATS["max_reqs"] = 0
+
+
+def reset_impl_stats() -> None:
+    for key in IMPL_STATS:
+        IMPL_STATS[key] = 0
+
+
+def _ring_enabled() -> bool:
+    return os.environ.get("HCP_RING_ENABLED", "1") == "1"
+
+
+def _split_tokens() -> int:
+    return int(os.environ.get("HCP_RING_SPLIT_TOKENS", "0"))
+
+
+class HcpRingAttentionBackend(FlashAttentionBackend):
+    """Ring-attention backend.  ``get_name()`` stays ``"CUSTOM"``: vLLM's
+    Attention layer looks the backend up by that enum member."""
+
+    forward_includes_kv_cache_update: bool = False
+
+    @staticmethod
+    def get_name() -> str:
+        return "CUSTOM"
+
+    @staticmethod
+    def get_impl_cls() -> type["HcpRingAttentionImpl"]:
+        return HcpRingAttentionImpl
+
+    @staticmethod
+    def get_builder_cls() -> type[FlashAttentionMetadataBuilder]:
+        return FlashAttentionMetadataBuilder
+
+    @staticmethod
+    def get_kv_cache_shape(num_blocks: int, block_size: int, num_kv_heads: int, head_size: int,
+                           cache_dtype_str: str = "auto") -> tuple[int, ...]:
+        if block_size % 16 != 0:
+            raise ValueError("Block size must be a multiple of 16.")
+        return (num_blocks, num_kv_heads, block_size, 2 * head_size)
+
+    @staticmethod
+    def get_kv_cache_stride_order(include_num_layers_dimension: bool = False) -> tuple[int, ...]:
+        return (0, 1, 2, 3, 4) if include_num_layers_dimension else (0, 1, 2, 3)
+
+
+class HcpRingAttentionImpl(AttentionImpl):
+    """Local (causal, paged) + transient peer (non-causal) attention with the
+    LSE merge fused, on the B200 kernels.  Same constructor contract as the
+    reference (``ring_backend.py:464-498``)."""
+
+    def __init__(self, num_heads: int, head_size: int, scale: float, num_kv_heads: int | None = None,
+                 alibi_slopes: list[float] | None = None, sliding_window: int | None = None,
+                 kv_cache_dtype: str = "auto", logits_soft_cap: float | None = None,
+                 attn_type: str = AttentionType.DECODER,
+                 kv_sharing_target_layer_name: str | None = None, **kwargs) -> None:
+        self.num_heads = num_heads
+        self.head_size = head_size
+        self.scale = float(scale)
+        self.num_kv_heads = num_kv_heads if num_kv_heads is not None else num_heads
+        self.kv_cache_dtype = kv_cache_dtype
+        self.attn_type = attn_type
+        self.kv_sharing_target_layer_name = kv_sharing_target_layer_name
+        self.supports_quant_query_input = False
+        if alibi_slopes is not None:
+            raise NotImplementedError("HCP ring backend: ALiBi not supported")
+        if logits_soft_cap:
+            raise NotImplementedError("HCP ring backend: soft cap not supported")
+        if sliding_window is not None:
+            # The reference serves windows with its fp32 torch path; this
+            # backend has no CPU path and its kernels have no window mask.
+            raise NotImplementedError("HCP ring backend: sliding window not supported")
+        if kv_cache_dtype not in ("auto", "bfloat16", "float16"):
+            raise NotImplementedError(f"HCP ring backend: kv cache dtype {kv_cache_dtype}")
+        if head_size not in (64, 128):
+            raise NotImplementedError("HCP ring backend: head_size must be 64 or 128")
+        self.sliding_window = None
+        self.num_queries_per_kv = self.num_heads // self.num_kv_heads
+
+    # -- KV cache update -----------------------------------------------------
+    def do_kv_cache_update(self, layer: torch.nn.Module, key: torch.Tensor, value: torch.Tensor,
+                           kv_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+        """Scatter this step's K/V into the paged cache (``hcp_kv_cache_update``;
+        the reference's torch index_put, ``ring_backend.py:501-539``)."""
+        if self.attn_type in (AttentionType.ENCODER_ONLY, AttentionType.ENCODER):
+            return
+        n = slot_mapping.shape[0]
+        if n == 0:
+            return
+        sm = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+        ops.kv_cache_update(key[:n], value[:n], kv_cache, sm.contiguous())
+        IMPL_STATS["cache_update_cuda"] += 1
+
+    # -- forward -------------------------------------------------------------
+    @staticmethod
+    def _host_meta(attn_metadata):
+        """query_start_loc, seq_lens and first block ids on the host: one
+        device-to-host sync per engine step (all layers share the metadata)."""
+        cached = getattr(attn_metadata, "_hcp_host_meta", None)
+        if cached is not None:
+            return cached
+        qsl = attn_metadata.query_start_loc.tolist()
+        seq_lens = attn_metadata.seq_lens.tolist()
+        bt0 = attn_metadata.block_table[: len(seq_lens), 0].tolist()
+        cached = (qsl, seq_lens, bt0)
+        try:
+            attn_metadata._hcp_host_meta = cached
+        except (AttributeError, TypeError):
+            pass
+        return cached
+
+    def _peers_for_layer(self, layer_name: str, seq_lens, bt0) -> dict:
+        peers: dict[int, list] = {}
+        if not _ring_enabled():
+            return peers
+        for r in range(len(seq_lens)):
+            ck_list = PEER_REQ_MAP.get(int(bt0[r]))
+            if ck_list is None and len(seq_lens) == 1:
+                # single-request fallback, as the reference (ring_backend.py:746-755)
+                chunks = {key[0] for key in PEER_KV_STAGING}
+                if len(chunks) == 1:
+                    ck_list = [next(iter(chunks))]
+            if not ck_list:
+                continue
+            parts = []
+            for ck in ck_list:
+                kv = PEER_KV_STAGING.get((ck, layer_name))
+                if kv is None:
+                    parts = None
+                    break
+                parts.append(kv)
+            if parts is None:
+                logger.warning("HCP ring: request mapped to chunks %s but staging incomplete at layer %s; "
+                               "using the local path", ck_list, layer_name)
+                continue
+            peers[r] = parts
+        return peers
+
+    def forward(self, layer: torch.nn.Module, query: torch.Tensor, key: torch.Tensor,
+                value: torch.Tensor, kv_cache: torch.Tensor, attn_metadata, output: torch.Tensor,
+                output_scale: torch.Tensor | None = None,
+                output_block_scale: torch.Tensor | None = None) -> torch.Tensor:
+        if output_scale is not None or output_block_scale is not None:
+            raise NotImplementedError("fused output quant not supported")
+        if attn_metadata is None:
+            return output.fill_(0)  # profiling run
+        assert self.attn_type == AttentionType.DECODER, "HCP ring backend supports decoder attention only"
+        num_actual = attn_metadata.num_actual_tokens
+        q = query[:num_actual]
+        out = output[:num_actual]
+        qsl, seq_lens, bt0 = self._host_meta(attn_metadata)
+        BATCH_STATS["max_reqs"] = max(BATCH_STATS["max_reqs"], len(seq_lens))
+        layer_name = getattr(layer, "layer_name", "")
+        peers = self._peers_for_layer(layer_name, seq_lens, bt0)
+        block_size = kv_cache.shape[2]
+        split = _split_tokens() if _ring_enabled() else 0
+        plan = plan_layer(qsl, seq_lens, block_size, peers, split)
+        if misaligned_paged_starts(plan, block_size):
+            raise ValueError("HCP ring backend: peer prefix length must be a multiple of the block size")
+        k_a = v_a = None
+        if plan.peer_parts:
+            if len(plan.peer_parts) == 1:
+                k_a, v_a = plan.peer_parts[0]
+            else:
+                # several staged chunks (or requests): one peer arena per layer
+                k_a = torch.cat([k for k, _ in plan.peer_parts], dim=0)
+                v_a = torch.cat([v for _, v in plan.peer_parts], dim=0)
+                IMPL_STATS["peer_concat"] += 1
+        block_table = attn_metadata.block_table
+        if block_table.dtype != torch.int32:
+            block_table = block_table.to(torch.int32)
+        if plan.work.shape[0]:
+            ops.ring_attn_fwd(q, plan.work, scale=self.scale, num_kv_heads=self.num_kv_heads, out=out,
+                              k_a=k_a, v_a=v_a, kv_cache=kv_cache, block_table=block_table)
+            IMPL_STATS["attn_cuda"] += 1
+        if plan.decode.shape[0]:
+            ops.decode_splitkv(q, plan.decode, scale=self.scale, num_kv_heads=self.num_kv_heads,
+                               out=out, peer_k=k_a, peer_v=v_a, kv_cache=kv_cache,
+                               block_table=block_table)
+            IMPL_STATS["decode_cuda"] += 1
+        return output

@@ -27,7 +27,20 @@ from . import ops
 from .ring_schedule import RingPlan, plan_balanced
 
 
+def _cuda_attn(q, work, *, scale, num_kv_heads, out, lse, **src):
+    ops.ring_attn_fwd(q, work, scale=scale, num_kv_heads=num_kv_heads, out=out, lse=lse, **src)
+
+
+def _cuda_merge(out, prefix_o, prefix_lse, suffix_o, suffix_lse, out_lse):
+    ops.merge_attn_states(out, prefix_o, prefix_lse, suffix_o, suffix_lse, out_lse)
+
+
 class RingPrefill:
+    # The device ops.  Tests of the host-side schedule and communication
+    # substitute CPU checkers here; the product always runs the CUDA ops.
+    attn_fn = staticmethod(_cuda_attn)
+    merge_fn = staticmethod(_cuda_merge)
+
     def __init__(self, seq_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
                  scale: float, device: torch.device, dtype: torch.dtype = torch.bfloat16,
                  group=None, balance: bool = True):
@@ -68,8 +81,8 @@ class RingPrefill:
 
     # ------------------------------------------------------------------ helpers
     def _attn(self, q, items, out, lse, **src):
-        ops.ring_attn_fwd(q, ops.make_work(items), scale=self.scale, num_kv_heads=self.Hkv,
-                          out=out, lse=lse, **src)
+        self.attn_fn(q, ops.make_work(items), scale=self.scale, num_kv_heads=self.Hkv,
+                     out=out, lse=lse, **src)
         self.launches += 1
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
@@ -126,8 +139,8 @@ class RingPrefill:
         if self.give:
             gv = self.give
             o_lse = None if lse is None else lse[:, :gv]
-            ops.merge_attn_states(out[:gv], self.acc[:gv], self.acc_lse[:, :gv], self.o_part,
-                                  self.lse_part, o_lse)
+            self.merge_fn(out[:gv], self.acc[:gv], self.acc_lse[:, :gv], self.o_part,
+                          self.lse_part, o_lse)
             self.launches += 1
         return out
 

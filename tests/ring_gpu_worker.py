@@ -1,0 +1,77 @@
+"""Worker for test_ring_multi_gpu.py (run under torchrun, one rank per GPU).
+
+Each rank runs RingPrefill.forward on its contiguous chunk of a seeded
+sequence over NCCL; rank 0 gathers the chunks and compares them with the
+single-GPU fused kernel over the whole sequence and with the CPU oracle on
+sampled rows.  Prints one JSON line on rank 0 and exits non-zero on mismatch.
+"""
+
+import datetime
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from hcp_vllm_plugin_b200 import _capi, ops  # noqa: E402
+from hcp_vllm_plugin_b200.ring_runner import RingPrefill  # noqa: E402
+from oracle import ring_oracle as ro  # noqa: E402
+
+H, HKV, D = 28, 4, 128
+
+
+def main():
+    seq = int(sys.argv[1]) if len(sys.argv) > 1 else 16384
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    g = torch.Generator(device="cpu").manual_seed(0)
+    q = torch.randn(seq, H, D, generator=g).bfloat16()
+    k = torch.randn(seq, HKV, D, generator=g).bfloat16()
+    v = torch.randn(seq, HKV, D, generator=g).bfloat16()
+    runner = RingPrefill(seq, H, HKV, D, D ** -0.5, dev)
+    c = runner.chunk
+    sl = slice(rank * c, (rank + 1) * c)
+    out = torch.empty(c, H, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(H, c, dtype=torch.float32, device=dev)
+    for _ in range(2):  # twice: buffers are reused across layers
+        runner.forward(q[sl].to(dev), k[sl].to(dev), v[sl].to(dev), out, lse)
+    outs = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(outs, out)
+    lses = [torch.empty_like(lse) for _ in range(world)]
+    dist.all_gather(lses, lse)
+    ok = True
+    if rank == 0:
+        full_o, full_lse = ops.ring_attn_with_lse(q.to(dev), k.to(dev), v.to(dev), D ** -0.5, 0)
+        got = torch.cat(outs).float()
+        got_lse = torch.cat(lses, 1)
+        d_out = (got - full_o.float()).abs()
+        tol = 2e-3 + 2.0 ** -7 * full_o.float().abs()
+        rows = np.unique(np.r_[np.linspace(0, seq - 1, 24).astype(int), [c - 1, c, seq - 1]])
+        qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
+        worst = 0.0
+        for r in rows:
+            o, _ = ro.attn_with_lse(qf[r:r + 1], kf[: r + 1], vf[: r + 1], D ** -0.5, r)
+            worst = max(worst, float(np.abs(got[r].cpu().numpy() - o[0]).max()))
+        res = {"world": world, "seq": seq, "give": runner.plan.give,
+               "max_vs_single_gpu": float(d_out.max()), "within_tol": bool((d_out <= tol).all()),
+               "lse_max": float((got_lse - full_lse).abs().max()), "oracle_rows_max": worst,
+               "device_status": _capi.device_status()}
+        ok = res["within_tol"] and res["lse_max"] <= 1e-3 and res["device_status"] == 0 and worst <= 2e-3 + 0.02
+        print(json.dumps(res), flush=True)
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.broadcast(flag, 0)
+    dist.barrier(device_ids=[local])
+    dist.destroy_process_group()
+    sys.exit(0 if flag.item() else 1)
+
+
+if __name__ == "__main__":
+    main()

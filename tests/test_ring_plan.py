@@ -1,0 +1,65 @@
+"""Host plan of a layer call (no GPU, no vLLM): the rows, segments and
+offsets the backend hands to the kernels follow the reference forward()."""
+
+import os
+
+import numpy as np
+import torch
+
+from hcp_vllm_plugin_b200 import _capi as C
+from hcp_vllm_plugin_b200.ring_plan import misaligned_paged_starts, plan_layer
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _peers_from_fixture(z):
+    peers = {}
+    for r in range(len(z["seq_lens"])):
+        n = int(z["peer_counts"][r])
+        if n:
+            peers[r] = [(torch.from_numpy(z[f"peer{r}_{c}_k"].view(np.int16)),
+                         torch.from_numpy(z[f"peer{r}_{c}_v"].view(np.int16))) for c in range(n)]
+    return peers
+
+
+def test_plan_matches_reference_split():
+    z = np.load(os.path.join(GOLD, "forward_case.npz"))
+    peers = _peers_from_fixture(z)
+    plan = plan_layer(z["query_start_loc"], z["seq_lens"], 16, peers)
+    # request 2 has a single query token -> decode kernel
+    assert plan.decode.shape[0] == 1
+    qr, pstart, plen, preq, lstart, llen = plan.decode[0]
+    assert (qr, preq, plen, lstart, llen) == (104, 2, 48, 48, 97 - 48)
+    w = {tuple(x[:2]): x for x in plan.work}
+    # request 0: tq=40, tk=72, staged 32 -> peer non-causal + local [32,72) causal offset 0
+    x = w[(0, 40)]
+    assert list(x[4:8]) == [C.HCP_SRC_A, 0, 32, -1]
+    assert list(x[8:12]) == [C.HCP_SRC_PAGED, 32, 40, 0]
+    # request 1: tq=64, tk=64, staged 32 -> n_a = 32 rows fully causal over all keys
+    x = w[(40, 32)]
+    assert list(x[4:8]) == [C.HCP_SRC_PAGED, 0, 64, 0]
+    x = w[(72, 32)]
+    assert list(x[4:8]) == [C.HCP_SRC_A, 32, 32, -1]
+    assert list(x[8:12]) == [C.HCP_SRC_PAGED, 32, 32, 0]
+    # request 3: no peer -> causal over its own keys at offset qpos0 = 0
+    x = w[(105, 24)]
+    assert list(x[4:8]) == [C.HCP_SRC_PAGED, 0, 24, 0]
+    # request 4: three ordered chunks concatenated into one peer segment
+    x = w[(129, 30)]
+    assert list(x[4:8]) == [C.HCP_SRC_A, 32 + 32 + 48, 64, -1]
+    assert list(x[8:12]) == [C.HCP_SRC_PAGED, 64, 30, 0]
+    assert plan.peer_rows == 32 + 32 + 48 + 64 and len(plan.peer_parts) == 6
+    assert not misaligned_paged_starts(plan, 16)
+    assert plan.stats["decode_rows"] == 1 and plan.stats["peer_requests"] == 4
+
+
+def test_plan_split_tokens_and_misalignment():
+    # HCP_RING_SPLIT_TOKENS mode: the peer prefix lives in the paged cache, so
+    # the merged result is causal attention over every key (one segment)
+    plan = plan_layer([0, 10], [50], 16, {}, split_tokens=20)
+    assert plan.work.shape[0] == 1
+    assert list(plan.work[0][4:8]) == [C.HCP_SRC_PAGED, 0, 50, 40]
+    # a staged prefix that is not block aligned cannot be read from the cache
+    k = torch.zeros(20, 2, 64)
+    plan = plan_layer([0, 10], [50], 16, {0: [(k, k)]})
+    assert misaligned_paged_starts(plan, 16)
