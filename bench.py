@@ -188,6 +188,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-balance", action="store_true")
+    ap.add_argument("--no-side", action="store_true")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -304,6 +305,8 @@ def main():
     if not args.no_e2e:
         e2e = run_e2e(args, runner, dev, chunk, L, barrier, max_over_ranks, world)
 
+    side = side_configs(dev, pk) if (world == 1 and not args.no_side) else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         dt, fl, threads = cpu_sample(seq, args.cpu_rows)
@@ -322,11 +325,81 @@ def main():
             "tflops": tflops, "pct_bf16_peak": 100.0 * tflops / peak_tf,
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clk,
+            "other_configs": side,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
+
+
+def side_configs(dev, pk):
+    """Device-timed BASELINE configs[1] (paged continuous-batch prefill) and
+    configs[2] (split-KV decode), reported beside the headline at N=1."""
+    import numpy as np
+    import torch
+
+    from hcp_vllm_plugin_b200 import _capi as C
+    from hcp_vllm_plugin_b200 import ops
+
+    res = {}
+    g = torch.Generator(device=dev).manual_seed(3)
+    scale = D ** -0.5
+
+    def timed(fn, n=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    # ---- configs[1]: 4 requests, local {512,1024,2048,3072} + 1024 peer each
+    lens, peer, bs = [512, 1024, 2048, 3072], 1024, 16
+    nbl = [(peer + L) // bs for L in lens]
+    num_blocks = sum(nbl)
+    perm = torch.randperm(num_blocks, generator=torch.Generator().manual_seed(1)).to(torch.int32)
+    bt = torch.zeros(len(lens), max(nbl), dtype=torch.int32)
+    o = 0
+    for r, n in enumerate(nbl):
+        bt[r, :n] = perm[o:o + n]
+        o += n
+    bt = bt.to(dev)
+    cache = torch.empty(num_blocks, HKV, bs, 2 * D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    qsl = np.concatenate([[0], np.cumsum(lens)])
+    q1 = torch.empty(int(qsl[-1]), H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    kp = torch.empty(len(lens) * peer, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    vp = torch.empty_like(kp).normal_(generator=g)
+    out1 = torch.empty_like(q1)
+    work = ops.make_work([(int(qsl[r]), L, r, int(qsl[r]), (C.HCP_SRC_A, r * peer, peer, -1),
+                           (C.HCP_SRC_PAGED, peer, L, 0)) for r, L in enumerate(lens)])
+    ms1 = timed(lambda: ops.ring_attn_fwd(q1, work, scale=scale, num_kv_heads=HKV, out=out1, k_a=kp,
+                                          v_a=vp, kv_cache=cache, block_table=bt))
+    fl1 = 4.0 * D * H * sum(L * (L + 1) // 2 + peer * L for L in lens)
+    res["cfg1_batch_prefill"] = {"ms": ms1, "tflops": fl1 / ms1 / 1e9,
+                                 "frac_of_bf16_burst": fl1 / ms1 / 1e9 / pk["bf16_tflops"]}
+    del cache, q1, kp, vp, out1
+
+    # ---- configs[2]: 64 x (32768 paged local + 32768 peer) single-token decode
+    B, LOC, PEER = 64, 32768, 32768
+    nb = LOC // bs
+    cache = torch.empty(B * nb, HKV, bs, 2 * D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    pk2 = torch.empty(B * PEER, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    pv2 = torch.empty_like(pk2).normal_(generator=g)
+    bt2 = torch.randperm(B * nb, generator=torch.Generator().manual_seed(2)).to(torch.int32).view(B, nb).to(dev)
+    q2 = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    out2 = torch.empty_like(q2)
+    seqs = np.array([(b, b * PEER, PEER, b, 0, LOC) for b in range(B)], np.int32)
+    ms2 = timed(lambda: ops.decode_splitkv(q2, seqs, scale=scale, num_kv_heads=HKV, out=out2, peer_k=pk2,
+                                           peer_v=pv2, kv_cache=cache, block_table=bt2))
+    byts = B * (LOC + PEER) * HKV * D * 2 * 2
+    res["cfg2_splitkv_decode"] = {"ms": ms2, "gbs": byts / ms2 / 1e6, "algorithmic_bytes": byts,
+                                  "frac_of_hbm": byts / ms2 / 1e6 / pk["hbm_gbs"]}
+    return res
 
 
 def run_e2e(args, runner, dev, chunk, L, barrier, max_over_ranks, world):
