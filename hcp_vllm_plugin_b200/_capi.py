@@ -19,6 +19,7 @@ STATUS_NAMES = {
     2: "HCP_ERR_UNSUPPORTED",
     3: "HCP_ERR_CUDA",
     4: "HCP_ERR_DEVICE",
+    5: "HCP_ERR_SCRATCH_LIMIT",
 }
 
 HCP_BF16, HCP_F16, HCP_F32 = 0, 1, 2
@@ -119,6 +120,7 @@ SIGNATURES = {
         ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     "hcp_ring_decode_splitkv": (ctypes.c_int, [ctypes.POINTER(HcpDecodeArgs), ctypes.c_void_p]),
     "hcp_decode_workspace_bytes": (ctypes.c_int64, [ctypes.POINTER(HcpDecodeArgs)]),
+    "hcp_ring_decode_splitkv_noalloc": (ctypes.c_int, [ctypes.POINTER(HcpDecodeArgs), ctypes.c_void_p]),
     "hcp_kv_cache_update": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,

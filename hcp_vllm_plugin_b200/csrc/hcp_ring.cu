@@ -546,3 +546,55 @@ extern "C" int hcp_kv_cache_update(const void* key, const void* value, int64_t n
   kv_cache_update_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
+
+// ---------------------------------------------------------------------------
+// Split-KV decode without allocation (hcp_ring_decode_splitkv_noalloc).
+//
+// Callers that own no device allocator, or whose HBM is already promised to a
+// paged KV cache, cannot hand in a workspace.  Their partials live in this
+// fixed array instead: it belongs to the library's device image, so every GPU
+// that loads the library keeps HCP_DECODE_NOALLOC_SCRATCH_BYTES of it until
+// the process exits, and no call allocates or frees device memory.  All
+// calls share it; overlapping calls race.
+// ---------------------------------------------------------------------------
+namespace {
+
+static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[HCP_DECODE_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of the array, per device ordinal
+
+// The host-side name of the array is not a device address: ask the runtime
+// for it once per device, with that device current.
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return HCP_ERR_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return HCP_OK;
+}
+
+}  // namespace
+
+extern "C" int hcp_ring_decode_splitkv_noalloc(const hcp_decode_args* a, void* stream) {
+  const int rc = validate_decode(a);
+  if (rc != HCP_OK) return rc;
+  if (a->num_seqs == 0) return HCP_OK;
+  // Every partial the merge step reads is written earlier in the same call,
+  // so the array needs no clearing between calls.
+  if (workspace_need(a, decode_chunk_keys(a)) > HCP_DECODE_NOALLOC_SCRATCH_BYTES)
+    return HCP_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int rc2 = noalloc_scratch_address(&scratch);
+  if (rc2 != HCP_OK) return rc2;
+  hcp_decode_args b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = HCP_DECODE_NOALLOC_SCRATCH_BYTES;
+  return hcp_ring_decode_splitkv(&b, stream);
+}

@@ -31,7 +31,8 @@ typedef enum hcp_status {
   HCP_ERR_INVALID = 1,      /* bad argument (null pointer, inconsistent sizes) */
   HCP_ERR_UNSUPPORTED = 2,  /* shape / dtype / device the kernels do not handle */
   HCP_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed */
-  HCP_ERR_DEVICE = 4        /* a kernel reported a device-side failure (timeout) */
+  HCP_ERR_DEVICE = 4,       /* a kernel reported a device-side failure (timeout) */
+  HCP_ERR_SCRATCH_LIMIT = 5 /* the call needs more fixed scratch than the library holds */
 } hcp_status;
 
 typedef enum hcp_dtype { HCP_BF16 = 0, HCP_F16 = 1, HCP_F32 = 2 } hcp_dtype;
@@ -194,6 +195,38 @@ int hcp_kv_cache_update(const void* key, const void* value, int64_t num_tokens,
                         const int64_t* slot_mapping, void* kv_cache, int64_t num_blocks,
                         int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
                         int32_t dtype, void* stream);
+
+/* Bytes of the fixed device array behind hcp_ring_decode_splitkv_noalloc. */
+#define HCP_DECODE_NOALLOC_SCRATCH_BYTES (16LL * 1024 * 1024)
+
+/*
+ * Split-KV decode that allocates nothing.  Same arguments, kernels and
+ * results as hcp_ring_decode_splitkv, except that args->workspace and
+ * args->workspace_bytes are ignored: the per-chunk partials go to a fixed
+ * 16 MiB array that is part of this library's device image.
+ *
+ * For callers that cannot allocate device memory when they decode: a host
+ * that talks to the library only through this C ABI and owns no device
+ * allocator, or a serving engine that has already handed (almost) all free
+ * HBM to its paged KV cache, where an extra allocation at decode time can
+ * fail or break the memory budget it planned.
+ *
+ * Limits and rules:
+ *  - every GPU that loads the library holds the 16 MiB array until the
+ *    process exits;
+ *  - a call whose partials need more than HCP_DECODE_NOALLOC_SCRATCH_BYTES
+ *    (hcp_decode_workspace_bytes(args)) returns HCP_ERR_SCRATCH_LIMIT and
+ *    launches nothing; a larger args->chunk_keys needs fewer partials;
+ *  - the first call on a device looks up the array's device address (once
+ *    per device, with that device current); make that first call before
+ *    any stream capture begins;
+ *  - all calls share the one array and it keeps the last call's contents;
+ *    nothing in it has to start at zero (each call writes every partial it
+ *    reads), but calls that overlap on the GPU (other streams, other host
+ *    threads) race on it: serialise them.
+ * No counterpart in the reference.
+ */
+int hcp_ring_decode_splitkv_noalloc(const hcp_decode_args* args, void* stream);
 
 /*
  * Device-side status word shared by all kernels of the library on the
