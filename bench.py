@@ -189,6 +189,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-balance", action="store_true")
     ap.add_argument("--no-side", action="store_true")
+    ap.add_argument("--kernel", choices=["fwd", "decode"], default=None,
+                    help="profiling mode: time one kernel on a small case and exit")
+    ap.add_argument("--decode-seqs", type=int, default=16)
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -198,6 +201,9 @@ def main():
         args.gpus = world
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.kernel is not None:
+        run_kernel(args)
         return
 
     import datetime
@@ -400,6 +406,57 @@ def side_configs(dev, pk):
     res["cfg2_splitkv_decode"] = {"ms": ms2, "gbs": byts / ms2 / 1e6, "algorithmic_bytes": byts,
                                   "frac_of_hbm": byts / ms2 / 1e6 / pk["hbm_gbs"]}
     return res
+
+
+def run_kernel(args):
+    """Profiling mode (`--kernel fwd|decode`): a few launches of one kernel on
+    a small case, timed with CUDA events; prints one line, no JSON.
+
+    fwd:    one causal `--seq` x `--seq` layer on contiguous q/k/v (configs[3]
+            at a single-launch size);
+    decode: `--decode-seqs` sequences of 32768 paged + 32768 peer keys
+            (configs[2] has 64)."""
+    import numpy as np
+    import torch
+
+    from hcp_vllm_plugin_b200 import _capi as C
+    from hcp_vllm_plugin_b200 import ops
+
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.kernel == "fwd":
+        seq = args.seq
+        q = torch.empty(seq, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        k = torch.empty(seq, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        v = torch.empty(seq, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        out = torch.empty_like(q)
+        work = ops.make_work([(0, seq, 0, 0, (C.HCP_SRC_A, 0, seq, 0), None)])
+        fn = lambda: ops.ring_attn_fwd(q, work, scale=D ** -0.5, num_kv_heads=HKV, out=out, k_a=k, v_a=v)
+        work_units, unit = 4.0 * D * H * causal_pairs(seq), "TFLOP/s"
+    else:
+        B, LOC, PEER, bs = args.decode_seqs, 32768, 32768, 16
+        nb = LOC // bs
+        cache = torch.empty(B * nb, HKV, bs, 2 * D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        pk = torch.empty(B * PEER, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        pv = torch.empty_like(pk).normal_(generator=g)
+        bt = torch.randperm(B * nb, generator=torch.Generator().manual_seed(0)).to(torch.int32).view(B, nb).to(dev)
+        q = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        out = torch.empty_like(q)
+        seqs = np.array([(b, b * PEER, PEER, b, 0, LOC) for b in range(B)], np.int32)
+        fn = lambda: ops.decode_splitkv(q, seqs, scale=D ** -0.5, num_kv_heads=HKV, out=out, peer_k=pk,
+                                        peer_v=pv, kv_cache=cache, block_table=bt)
+        work_units, unit = float(B * (LOC + PEER) * HKV * D * 4), "GB/s"
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    fn()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    rate = work_units / ms / (1e9 if unit == "TFLOP/s" else 1e6)
+    print(f"kernel={args.kernel} ms={ms:.3f} {unit}={rate:.1f} device_status={C.device_status()}", flush=True)
 
 
 def run_e2e(args, runner, dev, chunk, L, barrier, max_over_ranks, world):
