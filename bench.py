@@ -328,7 +328,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) q/k/v per layer)", "config": config(args),
-            "tflops": tflops, "pct_bf16_peak": 100.0 * tflops / peak_tf,
+            "tflops": tflops, "pct_bf16_peak": 100.0 * tflops / (peak_tf * world),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clk,
             "other_configs": side,
