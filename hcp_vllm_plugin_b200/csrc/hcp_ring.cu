@@ -547,6 +547,39 @@ extern "C" int hcp_kv_cache_update(const void* key, const void* value, int64_t n
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
+extern "C" int hcp_kv_cache_gather(const void* kv_cache, int64_t num_blocks, int32_t block_size,
+                                   int32_t num_kv_heads, int32_t head_dim, const int64_t* slot_mapping,
+                                   int64_t num_tokens, void* key, void* value, int64_t key_row_stride,
+                                   int64_t value_row_stride, int32_t dtype, void* stream) {
+  if (dtype != HCP_BF16 && dtype != HCP_F16) return HCP_ERR_UNSUPPORTED;
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || (head_dim % 8) != 0 || block_size <= 0 ||
+      num_blocks <= 0)
+    return HCP_ERR_INVALID;
+  if (num_tokens == 0) return HCP_OK;
+  const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if (key == nullptr || value == nullptr || slot_mapping == nullptr || kv_cache == nullptr ||
+      key_row_stride < row || value_row_stride < row || (key_row_stride % 8) != 0 ||
+      (value_row_stride % 8) != 0 || !aligned16(key) || !aligned16(value) || !aligned16(kv_cache))
+    return HCP_ERR_INVALID;
+  CacheGatherParams p;
+  p.cache = static_cast<const uint16_t*>(kv_cache);
+  p.slot_mapping = slot_mapping;
+  p.key = static_cast<uint16_t*>(key);
+  p.value = static_cast<uint16_t*>(value);
+  p.key_row_stride = key_row_stride;
+  p.value_row_stride = value_row_stride;
+  p.num_blocks = num_blocks;
+  p.num_tokens = num_tokens;
+  p.block_size = block_size;
+  p.num_kv_heads = num_kv_heads;
+  p.head_dim = head_dim;
+  const int64_t warps = num_tokens * num_kv_heads;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
+  kv_cache_gather_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
 // ---------------------------------------------------------------------------
 // Split-KV decode without allocation (hcp_ring_decode_splitkv_noalloc).
 //
@@ -597,4 +630,77 @@ extern "C" int hcp_ring_decode_splitkv_noalloc(const hcp_decode_args* a, void* s
   b.workspace = scratch;
   b.workspace_bytes = HCP_DECODE_NOALLOC_SCRATCH_BYTES;
   return hcp_ring_decode_splitkv(&b, stream);
+}
+
+// ---------------------------------------------------------------------------
+// In-box chunk transport: CUDA IPC export / open of a device buffer and a
+// copy-engine copy between GPUs (NVLink through NVSwitch).  A producer
+// exports the buffer holding its chunk's per-layer K/V; a consumer process on
+// any GPU of the box maps it and copies the layers it needs into its own HBM.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(ptr);
+  });
+  return fn;
+}
+
+}  // namespace
+
+extern "C" int hcp_ipc_export(const void* ptr, uint8_t* handle_out, int64_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr) return HCP_ERR_INVALID;
+  AddressRangeFn range = address_range_fn();
+  if (range == nullptr) return HCP_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return HCP_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return HCP_ERR_CUDA;
+  static_assert(sizeof(h) == HCP_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return HCP_OK;
+}
+
+extern "C" int hcp_ipc_open(const uint8_t* handle, int32_t device, void** base_out) {
+  if (handle == nullptr || base_out == nullptr || device < 0) return HCP_ERR_INVALID;
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) return HCP_ERR_CUDA;
+  if (cudaSetDevice(device) != cudaSuccess) return HCP_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return HCP_ERR_CUDA;
+  }
+  *base_out = p;
+  return HCP_OK;
+}
+
+extern "C" int hcp_ipc_close(void* base) {
+  if (base == nullptr) return HCP_ERR_INVALID;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
+extern "C" int hcp_peer_copy(void* dst, const void* src, int64_t bytes, void* stream) {
+  if (bytes < 0 || ((dst == nullptr || src == nullptr) && bytes > 0)) return HCP_ERR_INVALID;
+  if (bytes == 0) return HCP_OK;
+  return cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault,
+                         static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? HCP_OK
+             : HCP_ERR_CUDA;
 }

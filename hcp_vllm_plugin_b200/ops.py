@@ -270,6 +270,34 @@ def decode_splitkv(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, 
     del keep
 
 
+def kv_cache_gather(kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                    key: torch.Tensor | None = None,
+                    value: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """K/V rows of ``slot_mapping`` out of the paged cache (``hcp_kv_cache_gather``).
+
+    kv_cache [num_blocks, Hkv, block_size, 2*D]; slot_mapping [n] int64 on the
+    cache's device.  Returns key, value [n, Hkv, D] (allocated unless given);
+    rows of negative or out-of-range slots are zeros.
+    """
+    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be a contiguous int64 tensor")
+    if kv_cache.dim() != 4 or not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous [num_blocks, Hkv, block_size, 2*D] tensor")
+    nb, hkv, bs, d2 = kv_cache.shape
+    n = slot_mapping.shape[0]
+    if key is None:
+        key = torch.empty(n, hkv, d2 // 2, dtype=kv_cache.dtype, device=kv_cache.device)
+    if value is None:
+        value = torch.empty(n, hkv, d2 // 2, dtype=kv_cache.dtype, device=kv_cache.device)
+    if key.shape[0] < n or value.shape[0] < n or key.dtype != kv_cache.dtype or value.dtype != kv_cache.dtype:
+        raise ValueError("key/value must hold n rows of the cache's dtype")
+    rc = C.load().hcp_kv_cache_gather(
+        _ptr(kv_cache), nb, bs, hkv, d2 // 2, _ptr(slot_mapping), n, _ptr(key), _ptr(value),
+        _rows_heads(key, "key"), _rows_heads(value, "value"), _DT[kv_cache.dtype], _stream(kv_cache))
+    C.check(rc, "hcp_kv_cache_gather")
+    return key, value
+
+
 def kv_cache_update(key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tensor,
                     slot_mapping: torch.Tensor) -> None:
     """Paged scatter of new K/V rows (``hcp_kv_cache_update``).

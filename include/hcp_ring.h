@@ -196,6 +196,22 @@ int hcp_kv_cache_update(const void* key, const void* value, int64_t num_tokens,
                         int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
                         int32_t dtype, void* stream);
 
+/*
+ * Gather the K/V rows of slot_mapping (int64, device) out of the paged cache
+ * [num_blocks, Hkv, block_size, 2*D] into key/value [num_tokens, Hkv, D]
+ * (given row strides, elements).  Rows of slots < 0 or beyond the cache are
+ * written as zeros.
+ *
+ * Replaces: HcpRingKvConnector.save_kv_layer's pool -> chunk extraction
+ * (hcp_vllm_plugin/ring_connector.py:890-919, torch advanced index
+ * kv_layer[block_idxs, :, offsets] :909-910) in the
+ * [num_blocks, Hkv, block_size, 2*D] layout.
+ */
+int hcp_kv_cache_gather(const void* kv_cache, int64_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, const int64_t* slot_mapping,
+                        int64_t num_tokens, void* key, void* value, int64_t key_row_stride,
+                        int64_t value_row_stride, int32_t dtype, void* stream);
+
 /* Bytes of the fixed device array behind hcp_ring_decode_splitkv_noalloc. */
 #define HCP_DECODE_NOALLOC_SCRATCH_BYTES (16LL * 1024 * 1024)
 
@@ -227,6 +243,28 @@ int hcp_kv_cache_update(const void* key, const void* value, int64_t num_tokens,
  * No counterpart in the reference.
  */
 int hcp_ring_decode_splitkv_noalloc(const hcp_decode_args* args, void* stream);
+
+/*
+ * In-box chunk transport (CUDA IPC + copy engine over NVLink).
+ *
+ * hcp_ipc_export: IPC handle (HCP_IPC_HANDLE_BYTES bytes) of the device
+ *   allocation containing ptr, and ptr's byte offset inside it.
+ * hcp_ipc_open: map a handle exported by another process into this process
+ *   for `device` (peer access enabled lazily); *base_out = allocation base.
+ * hcp_ipc_close: unmap a base returned by hcp_ipc_open.
+ * hcp_peer_copy: stream-ordered copy of `bytes` between any two device
+ *   pointers of the box (local or mapped from a peer GPU).
+ *
+ * Replace: the HTTP prefill-KV store of HcpRingKvConnector
+ * (hcp_vllm_plugin/ring_connector.py:386-548: _start_http_server, _fetch,
+ * _remote_exists) for producers and consumers inside one box; the _READY
+ * marker (ring_connector.py:547-549, 777-792, 921-937) carries the handle.
+ */
+#define HCP_IPC_HANDLE_BYTES 64
+int hcp_ipc_export(const void* ptr, uint8_t* handle_out, int64_t* offset_out);
+int hcp_ipc_open(const uint8_t* handle, int32_t device, void** base_out);
+int hcp_ipc_close(void* base);
+int hcp_peer_copy(void* dst, const void* src, int64_t bytes, void* stream);
 
 /*
  * Device-side status word shared by all kernels of the library on the

@@ -221,6 +221,28 @@ def kv_cache_update(cache: np.ndarray, key: np.ndarray, value: np.ndarray,
         cache[b, :, o, d:] = value[i]
 
 
+def kv_cache_gather(cache: np.ndarray, slot_mapping: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """K, V [n, Hkv, D] of the given slots out of the paged cache.
+
+    Restates the producer's pool -> chunk extraction of
+    ``HcpRingKvConnector.save_kv_layer`` (``ring_connector.py:906-910``:
+    ``kv_layer[slot // block_size, :, slot % block_size]``) in the
+    ``[num_blocks, Hkv, block_size, 2*D]`` layout; rows of slots outside the
+    cache (or negative) are zeros.
+    """
+    nb, hkv, bs, d2 = cache.shape
+    d = d2 // 2
+    slot_mapping = np.asarray(slot_mapping, dtype=np.int64)
+    k = np.zeros((slot_mapping.shape[0], hkv, d), cache.dtype)
+    v = np.zeros_like(k)
+    for i, s in enumerate(slot_mapping):
+        if 0 <= s < nb * bs:
+            b, o = divmod(int(s), bs)
+            k[i] = cache[b, :, o, :d]
+            v[i] = cache[b, :, o, d:]
+    return k, v
+
+
 # ---------------------------------------------------------------------------
 # The per-request ring driver of HcpRingAttentionImpl.forward
 # ---------------------------------------------------------------------------
