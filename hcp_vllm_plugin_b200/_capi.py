@@ -133,6 +133,9 @@ SIGNATURES = {
     "hcp_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_void_p)]),
     "hcp_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
     "hcp_peer_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
+    "hcp_merge_attn_states_n": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     "hcp_get_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "hcp_reset_device_status": (ctypes.c_int, []),
     "hcp_version": (ctypes.c_char_p, []),

@@ -360,6 +360,37 @@ extern "C" int hcp_merge_attn_states(void* out, int32_t out_dtype, int64_t out_r
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
+extern "C" int hcp_merge_attn_states_n(void* out, int32_t out_dtype, int64_t out_row_stride,
+                                       float* out_lse, int64_t out_lse_stride, const float* states_o,
+                                       const float* states_lse, int32_t num_states, int64_t num_tokens,
+                                       int32_t num_heads, int32_t head_dim, void* stream) {
+  if (out == nullptr || states_o == nullptr || states_lse == nullptr) return HCP_ERR_INVALID;
+  if (out_dtype != HCP_BF16 && out_dtype != HCP_F16 && out_dtype != HCP_F32) return HCP_ERR_UNSUPPORTED;
+  if (num_states <= 0 || num_tokens < 0 || num_heads <= 0 || head_dim <= 0) return HCP_ERR_INVALID;
+  if (head_dim > 256) return HCP_ERR_UNSUPPORTED;
+  if (out_row_stride < static_cast<int64_t>(num_heads) * head_dim ||
+      (out_lse != nullptr && out_lse_stride < num_tokens))
+    return HCP_ERR_INVALID;
+  if (num_tokens == 0) return HCP_OK;
+  MergeNParams p;
+  p.out = out;
+  p.out_lse = out_lse;
+  p.states_o = states_o;
+  p.states_lse = states_lse;
+  p.out_stride = out_row_stride;
+  p.out_lse_stride = out_lse_stride;
+  p.num_tokens = num_tokens;
+  p.num_heads = num_heads;
+  p.head_dim = head_dim;
+  p.num_states = num_states;
+  p.out_dt = out_dtype;
+  const int64_t warps = num_tokens * num_heads;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
+  merge_states_n_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
 extern "C" int hcp_get_device_status(int32_t* status_out) {
   if (status_out == nullptr) return HCP_ERR_INVALID;
   if (cudaDeviceSynchronize() != cudaSuccess) return HCP_ERR_CUDA;

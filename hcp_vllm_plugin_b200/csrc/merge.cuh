@@ -67,4 +67,69 @@ __global__ void __launch_bounds__(256) merge_states_kernel(const MergeParams p) 
   if (lane == 0 && p.out_lse != nullptr) p.out_lse[h * p.out_lse_stride + tok] = lse;
 }
 
+// N-way merge of partial results stacked as o [N, T, H, D] fp32 and lse
+// [N, H, T] fp32 (one partial per KV shard): out = sum_i w_i o_i with
+// w_i = exp(lse_i - m) / sum_j exp(lse_j - m), m = max_i lse_i, and
+// lse = m + log(sum_j exp(lse_j - m)).  Empty partials (lse -inf, or +inf as
+// vLLM marks them) get weight 0; a row with no keys at all is 0 with lse -inf.
+struct MergeNParams {
+  void* out;
+  float* out_lse;
+  const float* states_o;
+  const float* states_lse;
+  long long out_stride;      // row stride (elements)
+  long long out_lse_stride;
+  long long num_tokens;
+  int num_heads;
+  int head_dim;
+  int num_states;
+  int out_dt;
+};
+
+__global__ void __launch_bounds__(256) merge_states_n_kernel(const MergeNParams p) {
+  const long long warp_global = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long rows = p.num_tokens * p.num_heads;
+  if (warp_global >= rows) return;
+  const long long tok = warp_global / p.num_heads;
+  const int h = static_cast<int>(warp_global - tok * p.num_heads);
+  const long long lse_state = static_cast<long long>(p.num_heads) * p.num_tokens;
+  const long long o_state = p.num_tokens * p.num_heads * p.head_dim;
+  float m = -INFINITY;
+  for (int i = 0; i < p.num_states; ++i) {
+    float l = p.states_lse[i * lse_state + h * p.num_tokens + tok];
+    if (l == INFINITY) l = -INFINITY;
+    m = fmaxf(m, l);
+  }
+  float tot = 0.f;
+  float acc[8];  // head_dim <= 256: at most 8 dims per lane
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  const long long row = (tok * p.num_heads + h) * p.head_dim;
+  if (m != -INFINITY) {
+    for (int i = 0; i < p.num_states; ++i) {
+      float l = p.states_lse[i * lse_state + h * p.num_tokens + tok];
+      if (l == INFINITY) l = -INFINITY;
+      const float w = expf(l - m);  // 0 for an empty partial
+      tot += w;
+      if (w == 0.f) continue;
+      const float* o = p.states_o + i * o_state + row;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int d = lane + 32 * j;
+        if (d < p.head_dim) acc[j] += w * o[d];
+      }
+    }
+  }
+  const float inv = tot > 0.f ? 1.f / tot : 0.f;
+  const long long oo = tok * p.out_stride + static_cast<long long>(h) * p.head_dim;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int d = lane + 32 * j;
+    if (d < p.head_dim) store_elem(p.out, p.out_dt, oo + d, acc[j] * inv);
+  }
+  if (lane == 0 && p.out_lse != nullptr)
+    p.out_lse[h * p.out_lse_stride + tok] = tot > 0.f ? m + logf(tot) : -INFINITY;
+}
+
 }  // namespace hcp

@@ -197,6 +197,27 @@ def merge_attn_states(
     C.check(rc, "hcp_merge_attn_states")
 
 
+def merge_attn_states_n(output: torch.Tensor, states_o: torch.Tensor, states_lse: torch.Tensor,
+                        output_lse: torch.Tensor | None = None) -> None:
+    """N-way LSE merge (``hcp_merge_attn_states_n``): states_o [N, T, H, D] and
+    states_lse [N, H, T] float32 contiguous -> output [T, H, D] (and output_lse
+    [H, T])."""
+    n, t, h, d = states_o.shape
+    if states_o.dtype != torch.float32 or states_lse.dtype != torch.float32:
+        raise ValueError("states must be float32")
+    if not states_o.is_contiguous() or not states_lse.is_contiguous() or tuple(states_lse.shape) != (n, h, t):
+        raise ValueError("states_o [N, T, H, D] and states_lse [N, H, T] must be contiguous")
+    if tuple(output.shape) != (t, h, d):
+        raise ValueError("output must be [T, H, D]")
+    if output_lse is not None and (output_lse.dtype != torch.float32 or output_lse.stride(1) != 1):
+        raise ValueError("output_lse must be float32 with unit column stride")
+    rc = C.load().hcp_merge_attn_states_n(
+        _ptr(output), _DT[output.dtype], _rows_heads(output, "output"), _ptr(output_lse),
+        0 if output_lse is None else output_lse.stride(0), _ptr(states_o), _ptr(states_lse), n, t, h, d,
+        _stream(output))
+    C.check(rc, "hcp_merge_attn_states_n")
+
+
 DECODE_FIELDS = 6  # q_row, peer_start, peer_len, paged_req, local_start, local_len
 
 _workspaces: dict = {}

@@ -163,6 +163,23 @@ typedef struct hcp_decode_args {
 } hcp_decode_args;
 
 /*
+ * N-way LSE merge of per-shard partials: states_o [num_states, T, H, D] fp32
+ * and states_lse [num_states, H, T] fp32 (natural log; -inf or +inf = empty
+ * partial), both contiguous -> out [T, H, D] (row stride out_row_stride,
+ * dtype out_dtype) and, if out_lse != NULL, the merged lse [H, T] (row
+ * stride out_lse_stride).  head_dim <= 256.
+ *
+ * Replaces: the decode ring's accumulator chain - _merge_pair
+ * (hcp_vllm_plugin/ring_decode.py:46-61) applied once per hop in
+ * RingDecodeNode.handle_packet (ring_decode.py:187-259) - with one launch
+ * over all shards' partials.
+ */
+int hcp_merge_attn_states_n(void* out, int32_t out_dtype, int64_t out_row_stride, float* out_lse,
+                            int64_t out_lse_stride, const float* states_o, const float* states_lse,
+                            int32_t num_states, int64_t num_tokens, int32_t num_heads,
+                            int32_t head_dim, void* stream);
+
+/*
  * Split-KV decode over a paged local segment plus a contiguous peer segment,
  * batch-merged (all sequences in one launch), LSE-merged across chunks.
  * Needs hcp_decode_workspace_bytes(args) bytes of device workspace.

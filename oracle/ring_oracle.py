@@ -348,6 +348,21 @@ def ring_forward(batch: RingBatch, round_to_bf16: bool = True) -> np.ndarray:
 # ---------------------------------------------------------------------------
 # Decode growth assignment (accumulator ring)
 # ---------------------------------------------------------------------------
+def merge_chain(states_o, states_lse) -> tuple[np.ndarray, np.ndarray]:
+    """Accumulate partials in ring order, as the decode ring's packet does.
+
+    ``states_o`` [N, T, H, D], ``states_lse`` [N, H, T]: the accumulator starts
+    as partial 0 and every later partial is merged into it
+    (``RingDecodeNode.handle_packet``, ``ring_decode.py:246-247``), each merge
+    with :func:`merge_attn_states` (empty partials, lse +/-inf, weigh 0).
+    """
+    o = np.asarray(states_o[0], np.float32)
+    lse = np.asarray(states_lse[0], np.float32)
+    for i in range(1, len(states_o)):
+        o, lse = merge_attn_states(o, lse, states_o[i], states_lse[i])
+    return o, lse
+
+
 def growth_assignee(pos: int, ring_size: int, policy: str = "rr") -> int:
     """Ring node that keeps the KV of the decode token at global ``pos``.
 
