@@ -13,7 +13,11 @@ without its per-request launches:
   causally (``:811-818``); the rest attend the peer keys (non-causal) and the
   local keys ``[peer_end, seq_len)`` causally at offset
   ``qpos0 + n_a - peer_end``, merged by LSE (``:819-832``) - here in one pass;
-* a request with a single query token goes to the split-KV decode kernel.
+* a request with a single query token goes to the split-KV decode kernel;
+* ``HCP_RING_SPLIT_TOKENS`` (single-instance validation, ``:776-778``): with
+  no staged peer the first ``split`` keys of the request's own paged cache
+  play the peer chunk - a non-causal paged segment merged with the causal
+  remainder in the same launch (``split`` must be block aligned).
 
 No vLLM import: the plan is plain integers and is tested on CPU.
 """
@@ -61,6 +65,7 @@ def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_to
         chunks = peers.get(r)
         peer_end = 0
         peer_off = 0
+        split_mode = False
         if chunks:
             peer_len = sum(int(k.shape[0]) for k, _ in chunks)
             peer_end = min(peer_len, tk)
@@ -69,12 +74,11 @@ def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_to
             arena += peer_len
             stats["peer_requests"] += 1
         elif split_tokens > 0:
-            # The peer prefix lives in the local cache: peer (non-causal) plus
-            # local (causal) merged is exactly causal attention over all keys.
-            peer_end = 0
+            peer_end = min(split_tokens, tk)
+            split_mode = True
         if tq == 1 and decode_kernel:
             stats["decode_rows"] += 1
-            if peer_end > 0:
+            if peer_end > 0 and not split_mode:
                 # query at position tk-1: every key is visible
                 dec.append([qs, peer_off, peer_end, r, peer_end, tk - peer_end])
             else:
@@ -90,8 +94,8 @@ def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_to
         if n_a < tq:
             local = tk - peer_end
             seg_local = [HCP_SRC_PAGED, peer_end, local, qpos0 + n_a - peer_end] if local > 0 else [0, 0, 0, 0]
-            work.append([qs + n_a, tq - n_a, r, qs + n_a,
-                         HCP_SRC_A, peer_off, peer_end, -1, *seg_local])
+            seg_peer = [HCP_SRC_PAGED, 0, peer_end, -1] if split_mode else [HCP_SRC_A, peer_off, peer_end, -1]
+            work.append([qs + n_a, tq - n_a, r, qs + n_a, *seg_peer, *seg_local])
     return LayerPlan(
         work=np.array(work, dtype=np.int32).reshape(-1, 12),
         decode=np.array(dec, dtype=np.int32).reshape(-1, 6),

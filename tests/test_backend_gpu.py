@@ -84,3 +84,50 @@ def test_backend_kv_cache_update_and_profile_run():
     out = torch.ones(3, 28, 128, dtype=torch.bfloat16, device=dev)
     impl.forward(None, out, None, None, cache, None, out)  # profiling run: zero fill
     assert (out == 0).all()
+
+
+def test_backend_split_tokens_matches_oracle(monkeypatch):
+    """HCP_RING_SPLIT_TOKENS validation mode: the first `split` keys of each
+    request's own paged cache act as the peer chunk (non-causal, fused with
+    the causal rest in one launch); compared with the oracle's restatement
+    of the reference forward with the same split."""
+    from hcp_vllm_plugin_b200 import ring_backend as rb
+    dev = torch.device("cuda:0")
+    g = np.random.default_rng(9)
+    h, hkv, d, bs, split = 28, 4, 128, 16, 256
+    reqs = [(300, 700), (40, 300), (1, 513), (200, 200), (77, 260)]  # (tq, tk)
+    nb_req = [(tk + bs - 1) // bs for _, tk in reqs]
+    num_blocks = sum(nb_req) + 5
+    perm = g.permutation(num_blocks)
+    bt = np.zeros((len(reqs), max(nb_req)), np.int32)
+    o = 0
+    for r, n in enumerate(nb_req):
+        bt[r, :n] = perm[o:o + n]
+        o += n
+    cache = ro.round_bf16(g.standard_normal((num_blocks, hkv, bs, 2 * d)).astype(np.float32))
+    qsl = np.cumsum([0] + [tq for tq, _ in reqs])
+    query = ro.round_bf16(g.standard_normal((int(qsl[-1]), h, d)).astype(np.float32))
+    batch = ro.RingBatch(query=query, cache=cache, block_table=bt, query_start_loc=qsl,
+                         seq_lens=np.array([tk for _, tk in reqs]), scale=d ** -0.5, split_tokens=split)
+    want = ro.ring_forward(batch)
+
+    def t16(a):
+        return torch.from_numpy(np.asarray(a, np.float32)).to(torch.bfloat16).to(dev)
+
+    monkeypatch.setenv("HCP_RING_SPLIT_TOKENS", str(split))
+    rb.clear_peer_kv()
+    rb.reset_impl_stats()
+    impl = rb.HcpRingAttentionImpl(h, d, d ** -0.5, hkv)
+    meta = types.SimpleNamespace(
+        num_actual_tokens=int(qsl[-1]),
+        query_start_loc=torch.tensor(qsl, dtype=torch.int32, device=dev),
+        seq_lens=torch.tensor([tk for _, tk in reqs], dtype=torch.int32, device=dev),
+        block_table=torch.from_numpy(bt).to(dev))
+    out = torch.zeros(int(qsl[-1]), h, d, dtype=torch.bfloat16, device=dev)
+    impl.forward(types.SimpleNamespace(layer_name="model.layers.0.self_attn.attn"), t16(query), None, None,
+                 t16(cache), meta, out)
+    torch.cuda.synchronize()
+    assert rb.IMPL_STATS["attn_cuda"] == 1 and rb.IMPL_STATS["decode_cuda"] == 1
+    got = out.float().cpu().numpy()
+    err = np.abs(got - want)
+    assert (err <= 2e-3 + 2.0 ** -7 * np.abs(want)).all(), f"max err {err.max():.3e}"

@@ -54,11 +54,25 @@ def test_plan_matches_reference_split():
 
 
 def test_plan_split_tokens_and_misalignment():
-    # HCP_RING_SPLIT_TOKENS mode: the peer prefix lives in the paged cache, so
-    # the merged result is causal attention over every key (one segment)
-    plan = plan_layer([0, 10], [50], 16, {}, split_tokens=20)
+    # HCP_RING_SPLIT_TOKENS mode: the first `split` keys of the request's own
+    # cache are the peer segment (non-causal), the rest causal at
+    # qpos0 + n_a - peer_end (ring_backend.py:776-832)
+    plan = plan_layer([0, 10], [50], 16, {}, split_tokens=32)
     assert plan.work.shape[0] == 1
-    assert list(plan.work[0][4:8]) == [C.HCP_SRC_PAGED, 0, 50, 40]
+    assert list(plan.work[0][:4]) == [0, 10, 0, 0]
+    assert list(plan.work[0][4:8]) == [C.HCP_SRC_PAGED, 0, 32, -1]
+    assert list(plan.work[0][8:12]) == [C.HCP_SRC_PAGED, 32, 18, 40 - 32]
+    # queries inside the split region (n_a = 32 - 20 = 12) stay fully causal
+    plan = plan_layer([0, 30], [50], 16, {}, split_tokens=32)
+    w = {tuple(x[:2]): x for x in plan.work}
+    assert list(w[(0, 12)][4:8]) == [C.HCP_SRC_PAGED, 0, 50, 20]
+    assert list(w[(12, 18)][4:8]) == [C.HCP_SRC_PAGED, 0, 32, -1]
+    assert list(w[(12, 18)][8:12]) == [C.HCP_SRC_PAGED, 32, 18, 20 + 12 - 32]
+    # a decode row keeps the single paged segment (same keys)
+    plan = plan_layer([0, 1], [50], 16, {}, split_tokens=32)
+    assert plan.work.shape[0] == 0 and list(plan.decode[0]) == [0, 0, 0, 0, 0, 50]
+    # a split that is not block aligned cannot start a paged segment
+    assert misaligned_paged_starts(plan_layer([0, 10], [50], 16, {}, split_tokens=20), 16)
     # a staged prefix that is not block aligned cannot be read from the cache
     k = torch.zeros(20, 2, 64)
     plan = plan_layer([0, 10], [50], 16, {0: [(k, k)]})
