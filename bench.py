@@ -8,6 +8,7 @@ rotate over NVLink every layer (``hcp_vllm_plugin_b200.ring_runner``).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...
+    python bench.py --rows            # the connector / decode-ring rows (opt-in)
 
 Prints one JSON line on rank 0.  ``value`` is whole-job tokens/s measured on
 the device (CUDA events, barrier + synchronize around the timed steps, max
@@ -192,6 +193,8 @@ def main():
     ap.add_argument("--kernel", choices=["fwd", "decode"], default=None,
                     help="profiling mode: time one kernel on a small case and exit")
     ap.add_argument("--decode-seqs", type=int, default=16)
+    ap.add_argument("--rows", action="store_true",
+                    help="measure the connector / decode-ring rows instead of the headline")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -204,6 +207,9 @@ def main():
         return
     if args.kernel is not None:
         run_kernel(args)
+        return
+    if args.rows:
+        run_rows(args, world, rank, local_rank)
         return
 
     import datetime
@@ -457,6 +463,208 @@ def run_kernel(args):
     ms = a.elapsed_time(b)
     rate = work_units / ms / (1e9 if unit == "TFLOP/s" else 1e6)
     print(f"kernel={args.kernel} ms={ms:.3f} {unit}={rate:.1f} device_status={C.device_status()}", flush=True)
+
+
+def run_rows(args, world, rank, local_rank):
+    """``--rows``: one JSON line with device-timed measurements of the rows
+    beside the forward kernel (CUDA events, max over ranks where collective):
+
+    f2_gather       pool -> chunk extraction (``hcp_kv_cache_gather``): a
+                    16384-token chunk out of each of 28 layers' paged caches
+                    (940 MB, more than L2), bytes read + written vs HBM peak;
+    f3_merge_n      N-way LSE merge of 8 fp32 partials, 4096 rows x 28 heads;
+    f3_ring_decode  RingDecode.step over all ranks: 64 requests x 65536
+                    context keys split over the ranks, one layer; per-step
+                    time and the K/V bytes scanned per second, all ranks;
+    f1_ipc_copy     (N >= 2) a 2 GiB chunk store exported by rank 0 with CUDA
+                    IPC, copied by rank 1 with the copy engine over NVLink;
+    f4_file_import  (N = 1) hcp-kv-v1 import of 4 layers x 16384 tokens
+                    through HcpFileConnector (files just written, so the read
+                    comes from the page cache)."""
+    import ctypes
+    import datetime
+    import shutil
+    import tempfile
+    import types
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from hcp_vllm_plugin_b200 import _capi as C
+    from hcp_vllm_plugin_b200 import ops
+    from hcp_vllm_plugin_b200.ring_decode import RingDecode
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    pk, pk_src = peaks()
+    res: dict = {}
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def timed(fn, n=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    if rank == 0:
+        try:  # f2: gather
+            L, T, bs = 28, 16384, 16
+            nb = T // bs
+            caches = [torch.empty(nb, HKV, bs, 2 * D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+                      for _ in range(L)]
+            slots = [(torch.randperm(nb, generator=torch.Generator().manual_seed(i))[:, None] * bs
+                      + torch.arange(bs)[None, :]).flatten().to(dev) for i in range(L)]
+            kk = torch.empty(T, HKV, D, dtype=torch.bfloat16, device=dev)
+            vv = torch.empty_like(kk)
+            ms = timed(lambda: [ops.kv_cache_gather(caches[i], slots[i], key=kk, value=vv) for i in range(L)], 5)
+            byts = L * 2 * (T * HKV * 2 * D * 2)
+            res["f2_gather"] = {"ms_28_layers": ms, "gbs": byts / ms / 1e6, "bytes": byts,
+                                "frac_of_hbm": byts / ms / 1e6 / pk["hbm_gbs"]}
+            del caches, slots, kk, vv
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            res["f2_gather"] = {"error": repr(e)}
+        try:  # f3: N-way merge
+            n, t = 8, 4096
+            so = torch.empty(n, t, H, D, device=dev).normal_(generator=g)
+            sl = torch.empty(n, H, t, device=dev).normal_(generator=g)
+            o = torch.empty(t, H, D, dtype=torch.bfloat16, device=dev)
+            ol = torch.empty(H, t, device=dev)
+            ms = timed(lambda: ops.merge_attn_states_n(o, so, sl, ol))
+            byts = so.numel() * 4 + sl.numel() * 4 + o.numel() * 2 + ol.numel() * 4
+            res["f3_merge_n"] = {"ms": ms, "gbs": byts / ms / 1e6, "frac_of_hbm": byts / ms / 1e6 / pk["hbm_gbs"]}
+            del so, sl, o, ol
+        except Exception as e:  # noqa: BLE001
+            res["f3_merge_n"] = {"error": repr(e)}
+
+    # f3: ring decode over all ranks
+    B, total, warm, steps = 64, 65536, 3, 10
+    chunk = total // world
+    rd = RingDecode(1, B, chunk + warm + steps + 1, H, HKV, D, D ** -0.5, dev)
+    for b in range(B):
+        base = b * rd.cap
+        rd.k[0, base:base + chunk].normal_(generator=g)
+        rd.v[0, base:base + chunk].normal_(generator=g)
+        rd.lens[0][b] = chunk
+    q = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    kn = torch.empty(B, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    vn = torch.empty_like(kn).normal_(generator=g)
+    out = torch.empty(B, H, D, device=dev)
+    owner = rank == rd.owner
+    for s in range(warm):
+        rd.step(0, [total + s] * B, q if owner else None, kn if owner else None, vn if owner else None,
+                out if owner else None)
+    barrier()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(warm, warm + steps):
+        rd.step(0, [total + s] * B, q if owner else None, kn if owner else None, vn if owner else None,
+                out if owner else None)
+    b_.record()
+    barrier()
+    ms = a.elapsed_time(b_) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kv_bytes = B * (total + warm + steps // 2) * HKV * D * 2 * 2
+    res["f3_ring_decode"] = {"ms_per_step": ms, "requests": B, "context_keys": total, "ranks": world,
+                             "kv_gbs_all_ranks": kv_bytes / ms / 1e6,
+                             "frac_of_hbm_all_ranks": kv_bytes / ms / 1e6 / (pk["hbm_gbs"] * world)}
+    del rd
+
+    if world > 1:  # f1: CUDA IPC copy from rank 0's store to rank 1
+        nbytes = 2 << 30
+        info = [None]
+        store = None
+        if rank == 0:
+            store = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            h = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_int64()
+            C.check(C.load().hcp_ipc_export(store.data_ptr(), h, ctypes.byref(off)), "hcp_ipc_export")
+            info = [(bytes(h).hex(), int(off.value))]
+        dist.broadcast_object_list(info, src=0)
+        res_ipc = None
+        if rank == 1:
+            base = ctypes.c_void_p()
+            C.check(C.load().hcp_ipc_open(bytes.fromhex(info[0][0]), local_rank, ctypes.byref(base)),
+                    "hcp_ipc_open")
+            dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            src = base.value + info[0][1]
+            st = torch.cuda.current_stream().cuda_stream
+            ms = timed(lambda: C.check(C.load().hcp_peer_copy(dst.data_ptr(), src, nbytes, st), "copy"), 5)
+            C.load().hcp_ipc_close(base.value)
+            res_ipc = {"ms_2GiB": ms, "gbs": nbytes / ms / 1e6}
+            del dst
+        obj = [res_ipc]
+        if world > 1:
+            dist.broadcast_object_list(obj, src=1)
+        res["f1_ipc_copy"] = obj[0]
+        barrier()
+        del store
+
+    if world == 1:  # f4: file import
+        tmp = tempfile.mkdtemp(prefix="hcp_kv_")
+        try:
+            from safetensors.torch import save_file
+            from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+
+            from hcp_vllm_plugin_b200.file_connector import HcpConnectorMetadata, HcpFileConnector, ReqMeta
+            L4, T, bs = 4, 16384, 16
+            with open(os.path.join(tmp, "meta.json"), "w") as f:
+                json.dump(dict(format="hcp-kv-v1", prompt_token_ids=list(range(T + 1)), seq_len=T + 1,
+                               num_layers=L4, num_kv_heads=HKV, head_dim=D, dtype="bfloat16"), f)
+            for i in range(L4):
+                save_file({"kv": torch.randn(T, 2, HKV, D).bfloat16()}, os.path.join(tmp, f"layer_{i}.safetensors"))
+            extra = {"hcp_kv_dir": tmp}
+            kvt = types.SimpleNamespace(get_from_extra_config=lambda k, d=None: extra.get(k, d))
+            hf = types.SimpleNamespace(hidden_size=H * D, num_attention_heads=H, num_hidden_layers=L4,
+                                       num_key_value_heads=HKV)
+            cfg = types.SimpleNamespace(kv_transfer_config=kvt, cache_config=types.SimpleNamespace(block_size=bs),
+                                        model_config=types.SimpleNamespace(hf_config=hf, dtype=torch.bfloat16))
+            conn = HcpFileConnector(cfg, KVConnectorRole.WORKER, None)
+            sm = torch.arange(T, dtype=torch.int64)
+            names = [f"model.layers.{i}.self_attn.attn" for i in range(L4)]
+            caches = {n: torch.zeros(T // bs + 8, HKV, bs, 2 * D, dtype=torch.bfloat16, device=dev) for n in names}
+            fc = types.SimpleNamespace(no_compile_layers={n: types.SimpleNamespace(kv_cache=c) for n, c in caches.items()})
+            walls = []
+            for _ in range(3):
+                conn.bind_connector_metadata(HcpConnectorMetadata(requests=[ReqMeta(sm, T)]))
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                conn.start_load_kv(fc)
+                for n in names:
+                    conn.wait_for_layer_load(n)
+                conn.wait_for_save()
+                torch.cuda.synchronize()
+                walls.append(time.perf_counter() - t0)
+            byts = L4 * T * 2 * HKV * D * 2
+            w = min(walls)
+            res["f4_file_import"] = {"s_4_layers": w, "gbs": byts / w / 1e9, "bytes": byts,
+                                     "timing": "host wall clock, files in the page cache"}
+        except Exception as e:  # noqa: BLE001
+            res["f4_file_import"] = {"error": repr(e)}
+        finally:
+            shutil.rmtree(tmp, ignore_errors=True)
+
+    if rank == 0:
+        print(json.dumps({"rows": res, "n_gpus": world, "peaks": pk_src, "device_status": C.device_status()}),
+              flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def run_e2e(args, runner, dev, chunk, L, barrier, max_over_ranks, world):

@@ -45,6 +45,14 @@ EncodeTiledFn encode_fn() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// log2(n) when n is a power of two, else -1
+int pow2_shift(int n) {
+  if (n <= 0 || (n & (n - 1)) != 0) return -1;
+  int s = 0;
+  while ((1 << s) != n) ++s;
+  return s;
+}
+
 // 128-byte-swizzled tiled map over a 16-bit tensor.  dims/box innermost first;
 // strides (bytes) for dims 1..rank-1.
 bool encode_map(CUtensorMap* m, bool f16, int rank, const void* base, const uint64_t* dims,
@@ -384,6 +392,8 @@ extern "C" int hcp_merge_attn_states_n(void* out, int32_t out_dtype, int64_t out
   p.head_dim = head_dim;
   p.num_states = num_states;
   p.out_dt = out_dtype;
+  p.vec_ok = aligned16(states_o) &&
+             (out_dtype != HCP_F32 || (aligned16(out) && (out_row_stride % 4) == 0)) ? 1 : 0;
   const int64_t warps = num_tokens * num_heads;
   const int64_t blocks = (warps * 32 + 255) / 256;
   if (blocks > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
@@ -571,10 +581,11 @@ extern "C" int hcp_kv_cache_update(const void* key, const void* value, int64_t n
   p.block_size = block_size;
   p.num_kv_heads = num_kv_heads;
   p.head_dim = head_dim;
-  const int64_t warps = num_tokens * num_kv_heads;
-  const int64_t blocks = (warps * 32 + 255) / 256;
-  if (blocks > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
-  kv_cache_update_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  p.bs_shift = pow2_shift(block_size);
+  const int64_t blocks = (num_tokens + kCacheTokPerBlock - 1) / kCacheTokPerBlock;
+  if (blocks > 0x7fffffff || num_kv_heads > 65535) return HCP_ERR_UNSUPPORTED;
+  kv_cache_update_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(num_kv_heads)), 256, 0,
+                           static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
@@ -604,10 +615,11 @@ extern "C" int hcp_kv_cache_gather(const void* kv_cache, int64_t num_blocks, int
   p.block_size = block_size;
   p.num_kv_heads = num_kv_heads;
   p.head_dim = head_dim;
-  const int64_t warps = num_tokens * num_kv_heads;
-  const int64_t blocks = (warps * 32 + 255) / 256;
-  if (blocks > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
-  kv_cache_gather_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  p.bs_shift = pow2_shift(block_size);
+  const int64_t blocks = (num_tokens + kCacheTokPerBlock - 1) / kCacheTokPerBlock;
+  if (blocks > 0x7fffffff || num_kv_heads > 65535) return HCP_ERR_UNSUPPORTED;
+  kv_cache_gather_kernel<<<dim3(static_cast<unsigned>(blocks), static_cast<unsigned>(num_kv_heads)), 256, 0,
+                           static_cast<cudaStream_t>(stream)>>>(p);
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 

@@ -84,6 +84,7 @@ struct MergeNParams {
   int head_dim;
   int num_states;
   int out_dt;
+  int vec_ok;                // 16-byte aligned partials (and fp32 output rows): float4 path allowed
 };
 
 __global__ void __launch_bounds__(256) merge_states_n_kernel(const MergeNParams p) {
@@ -95,6 +96,49 @@ __global__ void __launch_bounds__(256) merge_states_n_kernel(const MergeNParams 
   const int h = static_cast<int>(warp_global - tok * p.num_heads);
   const long long lse_state = static_cast<long long>(p.num_heads) * p.num_tokens;
   const long long o_state = p.num_tokens * p.num_heads * p.head_dim;
+  const long long row = (tok * p.num_heads + h) * p.head_dim;
+  const long long oo = tok * p.out_stride + static_cast<long long>(h) * p.head_dim;
+  if (p.vec_ok && p.num_states <= 32 && p.head_dim == 128) {
+    // lane i holds state i's LSE; weights by warp shuffles; each lane owns 4
+    // consecutive dims (float4 loads of every partial row)
+    float l = -INFINITY;
+    if (lane < p.num_states) {
+      l = p.states_lse[lane * lse_state + h * p.num_tokens + tok];
+      if (l == INFINITY) l = -INFINITY;
+    }
+    float m = l;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+    const float w = (m == -INFINITY || lane >= p.num_states) ? 0.f : expf(l - m);
+    float tot = w;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < p.num_states; ++i) {
+      const float wi = __shfl_sync(0xffffffffu, w, i);
+      if (wi == 0.f) continue;
+      const float4 o = reinterpret_cast<const float4*>(p.states_o + i * o_state + row)[lane];
+      acc.x += wi * o.x;
+      acc.y += wi * o.y;
+      acc.z += wi * o.z;
+      acc.w += wi * o.w;
+    }
+    const float inv = tot > 0.f ? 1.f / tot : 0.f;
+    const long long d0 = oo + 4 * lane;
+    if (p.out_dt == HCP_F32) {
+      reinterpret_cast<float4*>(static_cast<float*>(p.out) + d0)[0] =
+          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    } else {
+      store_elem(p.out, p.out_dt, d0 + 0, acc.x * inv);
+      store_elem(p.out, p.out_dt, d0 + 1, acc.y * inv);
+      store_elem(p.out, p.out_dt, d0 + 2, acc.z * inv);
+      store_elem(p.out, p.out_dt, d0 + 3, acc.w * inv);
+    }
+    if (lane == 0 && p.out_lse != nullptr)
+      p.out_lse[h * p.out_lse_stride + tok] = tot > 0.f ? m + logf(tot) : -INFINITY;
+    return;
+  }
+  // generic path: any state count, head_dim <= 256
   float m = -INFINITY;
   for (int i = 0; i < p.num_states; ++i) {
     float l = p.states_lse[i * lse_state + h * p.num_tokens + tok];
@@ -102,15 +146,14 @@ __global__ void __launch_bounds__(256) merge_states_n_kernel(const MergeNParams 
     m = fmaxf(m, l);
   }
   float tot = 0.f;
-  float acc[8];  // head_dim <= 256: at most 8 dims per lane
+  float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-  const long long row = (tok * p.num_heads + h) * p.head_dim;
   if (m != -INFINITY) {
     for (int i = 0; i < p.num_states; ++i) {
       float l = p.states_lse[i * lse_state + h * p.num_tokens + tok];
       if (l == INFINITY) l = -INFINITY;
-      const float w = expf(l - m);  // 0 for an empty partial
+      const float w = expf(l - m);
       tot += w;
       if (w == 0.f) continue;
       const float* o = p.states_o + i * o_state + row;
@@ -122,7 +165,6 @@ __global__ void __launch_bounds__(256) merge_states_n_kernel(const MergeNParams 
     }
   }
   const float inv = tot > 0.f ? 1.f / tot : 0.f;
-  const long long oo = tok * p.out_stride + static_cast<long long>(h) * p.head_dim;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int d = lane + 32 * j;
