@@ -122,17 +122,20 @@ class RingPrefill:
             dst = self._peer(s)
             send = [dist.P2POp(dist.isend, self.o_help, dst, group=g),
                     dist.P2POp(dist.isend, self.lse_help, dst, group=g)]
-        # 4. own rows [give, C) against peer chunks [0, x), merged with step 2
-        if x > 0 and self.give < c:
-            rows = c - self.give
-            self._attn(q, [(self.give, rows, 0, self.give, (A, 0, x * c, -1), None)], out, lse,
-                       k_a=self.k_all, v_a=self.v_all, merge_o=self.acc, merge_lse=self.acc_lse)
+        # The partial's return is issued before step 4 is launched: a NCCL
+        # call waits for the work already queued on the compute stream, so
+        # issued here it overlaps step 4 instead of following it.
         recv = []
         if self.give:
             src = self._peer(self.helper)
             recv = [dist.P2POp(dist.irecv, self.o_part, src, group=g),
                     dist.P2POp(dist.irecv, self.lse_part, src, group=g)]
         hs = dist.batch_isend_irecv(send + recv) if (send or recv) else []
+        # 4. own rows [give, C) against peer chunks [0, x), merged with step 2
+        if x > 0 and self.give < c:
+            rows = c - self.give
+            self._attn(q, [(self.give, rows, 0, self.give, (A, 0, x * c, -1), None)], out, lse,
+                       k_a=self.k_all, v_a=self.v_all, merge_o=self.acc, merge_lse=self.acc_lse)
         for h in hs:
             h.wait()
         # 5. owner: merge the helper's partial for rows [0, give)
