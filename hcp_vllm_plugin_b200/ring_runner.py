@@ -9,11 +9,17 @@ in the kernel epilogue.  The work plan (``ring_schedule.plan_balanced``)
 moves query rows from heavy to light ranks so 8 ranks stay balanced.
 
 Per layer on rank x (chunk C tokens, ``give`` rows handed to a helper):
-  1. async: all-gather K and V of this layer; owner -> helper: Q[0:give]
-  2. own chunk, causal (resident, overlaps step 1) -> fp32 partial (O, LSE)
-  3. helper: its partner's Q rows vs chunks [0, s) -> fp32 partial, sent back
-  4. rows [give, C) vs chunks [0, x), merged with step 2 in the epilogue
-  5. owner: rows [0, give): merge step 2 with the helper's partial
+  1. all-gather K and V of this layer; owner -> helper: Q[0:give]
+  2. ONE launch over every row this rank computes, fp32 out + LSE:
+       rows [give, C): peer chunks [0, x) (non-causal) and the own chunk
+                       (causal) in one online softmax - final values;
+       rows [0, give): the own chunk only (causal) - a partial;
+       helper rows:    the partner's Q rows vs its peer chunks [0, s).
+     The host orders CTAs heaviest first, so the long peer CTAs start first
+     and the short causal ones fill the end of the launch (separate launches
+     per part each ended in a partial wave of equally long CTAs).
+  3. helper: send its partial back; owner: merge rows [0, give) with it;
+     rows [give, C) are cast to the output dtype.
 Every rank issues the same collectives in the same order.
 """
 
@@ -67,12 +73,15 @@ class RingPrefill:
         if self.world > 1:
             self.k_all = torch.empty(self.world * c, num_kv_heads, head_dim, dtype=dtype, device=device)
             self.v_all = torch.empty_like(self.k_all)
-            self.acc = torch.empty(c, num_heads, head_dim, dtype=f32, device=device)
-            self.acc_lse = torch.empty(num_heads, c, dtype=f32, device=device)
+            # combined rows of the one launch: own chunk rows, then helper rows
+            rows = c + self.owner_give
+            self.q_comb = torch.empty(rows, num_heads, head_dim, dtype=dtype, device=device)
+            self.acc = torch.empty(rows, num_heads, head_dim, dtype=f32, device=device)
+            self.acc_lse = torch.empty(num_heads, rows, dtype=f32, device=device)
         if self.owner is not None:
             g = self.owner_give
-            self.q_help = torch.empty(g, num_heads, head_dim, dtype=dtype, device=device)
-            self.o_help = torch.empty(g, num_heads, head_dim, dtype=f32, device=device)
+            self.q_help = self.q_comb[c:]
+            self.o_help = self.acc[c:]
             self.lse_help = torch.empty(num_heads, g, dtype=f32, device=device)
         if self.give:
             self.o_part = torch.empty(self.give, num_heads, head_dim, dtype=f32, device=device)
@@ -95,54 +104,54 @@ class RingPrefill:
             self._attn(q, [(0, c, 0, 0, (A, 0, c, 0), None)], out, lse, k_a=k, v_a=v)
             return out
         g = self.group
-        # 1. ring rotation of this layer's K/V (NCCL on its own stream, NVLink)
+        give = self.give
+        # 1. this layer's K/V to every rank (NCCL, NVLink); Q rows to the helper
         hk = dist.all_gather_into_tensor(self.k_all, k, group=g, async_op=True)
         hv = dist.all_gather_into_tensor(self.v_all, v, group=g, async_op=True)
         p2p = []
-        if self.give:
-            p2p.append(dist.P2POp(dist.isend, q[: self.give], self._peer(self.helper), group=g))
+        if give:
+            p2p.append(dist.P2POp(dist.isend, q[:give], self._peer(self.helper), group=g))
         if self.owner is not None:
             p2p.append(dist.P2POp(dist.irecv, self.q_help, self._peer(self.owner), group=g))
         hq = dist.batch_isend_irecv(p2p) if p2p else []
-        # 2. resident chunk, causal: overlaps the rotation
-        if x == 0:
-            self._attn(q, [(0, c, 0, 0, (A, 0, c, 0), None)], out, lse, k_a=k, v_a=v)
-        else:
-            self._attn(q, [(0, c, 0, 0, (A, 0, c, 0), None)], self.acc, self.acc_lse, k_a=k, v_a=v)
-        hk.wait()
-        hv.wait()
-        for h in hq:
+        self.q_comb[:c].copy_(q)
+        for h in (hk, hv, *hq):
             h.wait()
-        # 3. helper: the partner's rows against its peer chunks [0, s)
+        # 2. one launch over all rows of this rank
+        own = (A, x * c, c, 0)                      # own chunk, causal
+        items = []
+        if give:
+            items.append((0, give, 0, 0, own, None))
+        if give < c:
+            if x > 0:
+                items.append((give, c - give, 0, give, (A, 0, x * c, -1), (A, x * c, c, give)))
+            else:
+                items.append((give, c - give, 0, give, (A, x * c, c, give), None))
+        if self.owner is not None:
+            items.append((c, self.owner_give, 0, c, (A, 0, self.owner * c, -1), None))
+        self._attn(self.q_comb, items, self.acc, self.acc_lse, k_a=self.k_all, v_a=self.v_all)
+        # 3. helper partial back to its owner; merges and the output cast
         send = []
         if self.owner is not None:
-            s, gq = self.owner, self.owner_give
-            self._attn(self.q_help, [(0, gq, 0, 0, (A, 0, s * c, -1), None)], self.o_help,
-                       self.lse_help, k_a=self.k_all, v_a=self.v_all)
-            dst = self._peer(s)
+            self.lse_help.copy_(self.acc_lse[:, c:])
+            dst = self._peer(self.owner)
             send = [dist.P2POp(dist.isend, self.o_help, dst, group=g),
                     dist.P2POp(dist.isend, self.lse_help, dst, group=g)]
-        # The partial's return is issued before step 4 is launched: a NCCL
-        # call waits for the work already queued on the compute stream, so
-        # issued here it overlaps step 4 instead of following it.
         recv = []
-        if self.give:
+        if give:
             src = self._peer(self.helper)
             recv = [dist.P2POp(dist.irecv, self.o_part, src, group=g),
                     dist.P2POp(dist.irecv, self.lse_part, src, group=g)]
         hs = dist.batch_isend_irecv(send + recv) if (send or recv) else []
-        # 4. own rows [give, C) against peer chunks [0, x), merged with step 2
-        if x > 0 and self.give < c:
-            rows = c - self.give
-            self._attn(q, [(self.give, rows, 0, self.give, (A, 0, x * c, -1), None)], out, lse,
-                       k_a=self.k_all, v_a=self.v_all, merge_o=self.acc, merge_lse=self.acc_lse)
+        if give < c:
+            out[give:].copy_(self.acc[give:c])
+            if lse is not None:
+                lse[:, give:].copy_(self.acc_lse[:, give:c])
         for h in hs:
             h.wait()
-        # 5. owner: merge the helper's partial for rows [0, give)
-        if self.give:
-            gv = self.give
-            o_lse = None if lse is None else lse[:, :gv]
-            self.merge_fn(out[:gv], self.acc[:gv], self.acc_lse[:, :gv], self.o_part,
+        if give:
+            o_lse = None if lse is None else lse[:, :give]
+            self.merge_fn(out[:give], self.acc[:give], self.acc_lse[:, :give], self.o_part,
                           self.lse_part, o_lse)
             self.launches += 1
         return out
