@@ -138,6 +138,7 @@ SIGNATURES = {
         ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     "hcp_get_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "hcp_reset_device_status": (ctypes.c_int, []),
+    "hcp_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_int64, ctypes.POINTER(ctypes.c_int32)]),
     "hcp_version": (ctypes.c_char_p, []),
 }
 

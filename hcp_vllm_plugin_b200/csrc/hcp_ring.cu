@@ -416,6 +416,20 @@ extern "C" int hcp_reset_device_status(void) {
   return cudaDeviceSynchronize() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
+extern "C" int hcp_selftest_bounded_wait(int64_t timeout_ns, int32_t* waited_out) {
+  if (timeout_ns <= 0 || timeout_ns > 2000000000ll || waited_out == nullptr) return HCP_ERR_INVALID;
+  int* d = nullptr;
+  if (cudaMalloc(&d, sizeof(int)) != cudaSuccess) return HCP_ERR_CUDA;
+  bounded_wait_selftest_kernel<<<1, 32>>>(static_cast<uint64_t>(timeout_ns), d);
+  int r = -1;
+  const bool ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess &&
+                  cudaMemcpy(&r, d, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess;
+  cudaFree(d);
+  if (!ok) return HCP_ERR_CUDA;
+  *waited_out = r;  // 0: the wait ran out as intended
+  return HCP_OK;
+}
+
 extern "C" const char* hcp_version(void) { return "hcp_ring 0.1.0 (sm_100a)"; }
 
 namespace {

@@ -70,6 +70,7 @@ enum : int {
   kErrWaitMma = 0x102,
   kErrWaitSoftmax = 0x103,
   kErrWaitDrain = 0x104,
+  kErrWaitSelftest = 0x1ff,
 };
 
 struct FwdParams {
@@ -105,8 +106,8 @@ struct FwdParams {
 
 // Bounded mbarrier wait.  Returns false when this CTA aborted (this wait ran
 // out of time, another role of the CTA gave up, or another CTA failed).
-__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                         int code) {
+__device__ __forceinline__ bool wait_bar_for(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                             int code, uint64_t timeout_ns) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = ptx::global_timer_ns();
   for (uint32_t it = 1;; ++it) {
@@ -117,13 +118,32 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile
         *abort_flag = 1;
         return false;
       }
-      if (ptx::global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (ptx::global_timer_ns() - t0 > timeout_ns) {
         *abort_flag = 1;
         atomicCAS(&g_device_status, 0, code);
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                         int code) {
+  return wait_bar_for(bar, parity, abort_flag, code, kWaitTimeoutNs);
+}
+
+// Self-test of the failure path: one thread waits, through the same bounded
+// wait as the kernels, on an mbarrier that nothing arrives on.  The wait runs
+// out after timeout_ns, records kErrWaitSelftest in g_device_status and the
+// kernel returns normally: no fault, the context stays usable.
+__global__ void bounded_wait_selftest_kernel(uint64_t timeout_ns, int* result) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;
+  abort_flag = 0;
+  ptx::mbar_init(ptx::smem_u32(&bar), 1);
+  ptx::fence_mbar_init();
+  const bool ok = wait_bar_for(ptx::smem_u32(&bar), 0, &abort_flag, kErrWaitSelftest, timeout_ns);
+  *result = ok ? 1 : 0;
 }
 
 // Bounded wait that ignores the abort flag: used at teardown for work that

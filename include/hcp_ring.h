@@ -293,6 +293,15 @@ int hcp_peer_copy(void* dst, const void* src, int64_t bytes, void* stream);
 int hcp_get_device_status(int32_t* status_out);
 int hcp_reset_device_status(void);
 
+/*
+ * Failure-path self-test: launches one thread that waits, through the
+ * kernels' own bounded mbarrier wait, on a barrier nothing arrives on, for
+ * timeout_ns (at most 2 s).  The wait runs out, the device status becomes
+ * 0x1ff and the kernel returns normally; *waited_out = 0 confirms that the
+ * wait gave up.  Synchronises the device.  No counterpart in the reference.
+ */
+int hcp_selftest_bounded_wait(int64_t timeout_ns, int32_t* waited_out);
+
 /* Library version string (static storage). */
 const char* hcp_version(void);
 

@@ -1,0 +1,64 @@
+"""Failure detection without a GPU fault.
+
+Every wait of the library's kernels is bounded: when it runs out, the kernel
+records a code in the device status word, gives up and returns, and kernels
+launched while a code is recorded do no work until the host resets it.  The
+self-test entry point waits on an mbarrier that nothing arrives on, through
+the kernels' own bounded wait, with a short limit; nothing faults, traps or
+hangs, and the context stays usable afterwards.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ring_oracle as ro
+
+pytestmark = pytest.mark.gpu
+
+
+def test_bounded_wait_runs_out_and_reports():
+    from hcp_vllm_plugin_b200 import _capi as C, ops
+
+    lib = C.load()
+    C.reset_device_status()
+    try:
+        _run(C, ops, lib)
+    finally:
+        C.reset_device_status()  # later tests must not inherit a recorded failure
+
+
+def _run(C, ops, lib):
+    waited = ctypes.c_int32(-1)
+    C.check(lib.hcp_selftest_bounded_wait(50_000_000, ctypes.byref(waited)), "hcp_selftest_bounded_wait")
+    assert waited.value == 0                      # the wait gave up
+    assert C.device_status() == 0x1FF             # and said so
+
+    # While a failure is recorded, launches do no work (fail fast) ...
+    g = torch.Generator().manual_seed(0)
+    tq, tk, h, hkv, d = 256, 512, 28, 4, 128
+    q = torch.randn(tq, h, d, generator=g).bfloat16().cuda()
+    k = torch.randn(tk, hkv, d, generator=g).bfloat16().cuda()
+    v = torch.randn(tk, hkv, d, generator=g).bfloat16().cuda()
+    out = torch.full((tq, h, d), 7.0, dtype=torch.bfloat16, device="cuda")
+    lse = torch.full((h, tq), 7.0, device="cuda")
+    work = ops.make_work([(0, tq, 0, 0, (C.HCP_SRC_A, 0, tk, tk - tq), None)])
+    ops.ring_attn_fwd(q, work, scale=d ** -0.5, num_kv_heads=hkv, out=out, lse=lse, k_a=k, v_a=v)
+    torch.cuda.synchronize()
+    assert torch.all(out == 7.0) and torch.all(lse == 7.0)
+    assert C.device_status() == 0x1FF
+
+    # ... and after the host resets the status the same launch is correct.
+    C.reset_device_status()
+    ops.ring_attn_fwd(q, work, scale=d ** -0.5, num_kv_heads=hkv, out=out, lse=lse, k_a=k, v_a=v)
+    torch.cuda.synchronize()
+    assert C.device_status() == 0
+    want, want_lse = ro.attn_with_lse(q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                      v.float().cpu().numpy(), d ** -0.5, tk - tq)
+    err = np.abs(out.float().cpu().numpy() - want)
+    assert np.all(err <= 2e-3 + 2.0 ** -7 * np.abs(want))
+    assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-3
