@@ -2,11 +2,10 @@
 
 Replaces the reference's HTTP peer-KV pull and neighbour accumulate-forward
 (``ring_connector.py:21-32, 777-859``) inside one 8xB200 box: every layer, the
-K/V chunks rotate around the ring over NVLink (NCCL ring all-gather on the
-process group's stream) while each rank attends its resident chunk causally;
-then the peer chunks, now in local HBM, are attended non-causally and merged
-in the kernel epilogue.  The work plan (``ring_schedule.plan_balanced``)
-moves query rows from heavy to light ranks so 8 ranks stay balanced.
+K/V chunks rotate around the ring over NVLink (NCCL ring all-gather), then
+the peer chunks, now in local HBM, and the resident chunk are attended in
+one launch.  The work plan (``ring_schedule.plan_balanced``) moves query
+rows from heavy to light ranks so 8 ranks stay balanced.
 
 Per layer on rank x (chunk C tokens, ``give`` rows handed to a helper):
   1. all-gather K and V of this layer; owner -> helper: Q[0:give]
