@@ -142,16 +142,22 @@ class RingDecode:
         kb = pay[nq:nq + nk].view(B, Hkv, D)
         vb = pay[nq + nk:].view(B, Hkv, D)
         lens = self.lens[layer]
+        mine, rows = [], []
         for b, pos in enumerate(positions):
             if growth_assignee(int(pos), self.world, self.policy) != self.rank:
                 continue
-            row = b * self.cap + lens[b]
             if lens[b] >= self.cap:
                 raise RuntimeError(f"request {b}: growth exceeds the capacity {self.cap} on rank {self.rank}")
-            self.k[layer, row].copy_(kb[b])
-            self.v[layer, row].copy_(vb[b])
+            mine.append(b)
+            rows.append(b * self.cap + lens[b])
             lens[b] += 1
             self.growth_positions[layer][b].append(int(pos))
+        if mine:
+            # every token this rank keeps, in one copy for K and one for V
+            src = torch.tensor(mine, dtype=torch.long).to(self.device, non_blocking=True)
+            dst = torch.tensor(rows, dtype=torch.long).to(self.device, non_blocking=True)
+            self.k[layer].index_copy_(0, dst, kb.index_select(0, src))
+            self.v[layer].index_copy_(0, dst, vb.index_select(0, src))
         o = self._part[:nq].view(B, H, D)
         lse = self._part[nq:].view(H, B)
         self.partial_fn(qb, self.k[layer], self.v[layer], lens, self.cap, scale=self.scale,
