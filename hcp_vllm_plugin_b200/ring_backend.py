@@ -248,20 +248,36 @@ class HcpRingAttentionImpl(AttentionImpl):
         qsl, seq_lens, bt0 = self._host_meta(attn_metadata)
         BATCH_STATS["max_reqs"] = max(BATCH_STATS["max_reqs"], len(seq_lens))
         layer_name = getattr(layer, "layer_name", "")
-        peers = self._peers_for_layer(layer_name, seq_lens, bt0)
+        peers = self._peers_for_layer(layer_name, seq_lens, bt0) if (PEER_REQ_MAP or PEER_KV_STAGING) else {}
         block_size = kv_cache.shape[2]
         split = _split_tokens() if _ring_enabled() else 0
-        plan = plan_layer(qsl, seq_lens, block_size, peers, split)
-        if misaligned_paged_starts(plan, block_size):
-            raise ValueError("HCP ring backend: peer prefix length must be a multiple of the block size")
+        # The plan depends on lengths only (requests, staged chunks), which
+        # every layer of a step shares: build it once per step and rebuild
+        # just this layer's list of staged tensors.
+        sig = (block_size, split,
+               tuple((r, tuple(int(k.shape[0]) for k, _ in ch)) for r, ch in sorted(peers.items())))
+        plans = getattr(attn_metadata, "_hcp_plans", None)
+        if plans is None:
+            plans = {}
+            try:
+                attn_metadata._hcp_plans = plans
+            except (AttributeError, TypeError):
+                pass
+        plan = plans.get(sig)
+        if plan is None:
+            plan = plan_layer(qsl, seq_lens, block_size, peers, split)
+            if misaligned_paged_starts(plan, block_size):
+                raise ValueError("HCP ring backend: peer prefix length must be a multiple of the block size")
+            plans[sig] = plan
+        parts = [kv for r in plan.part_requests for kv in peers[r]]
         k_a = v_a = None
-        if plan.peer_parts:
-            if len(plan.peer_parts) == 1:
-                k_a, v_a = plan.peer_parts[0]
+        if parts:
+            if len(parts) == 1:
+                k_a, v_a = parts[0]
             else:
                 # several staged chunks (or requests): one peer arena per layer
-                k_a = torch.cat([k for k, _ in plan.peer_parts], dim=0)
-                v_a = torch.cat([v for _, v in plan.peer_parts], dim=0)
+                k_a = torch.cat([k for k, _ in parts], dim=0)
+                v_a = torch.cat([v for _, v in parts], dim=0)
                 IMPL_STATS["peer_concat"] += 1
         block_table = attn_metadata.block_table
         if block_table.dtype != torch.int32:

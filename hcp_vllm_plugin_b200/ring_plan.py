@@ -38,6 +38,7 @@ class LayerPlan:
     peer_parts: list = field(default_factory=list)   # (k, v) tensors, in arena order
     peer_rows: int = 0
     stats: dict = field(default_factory=dict)
+    part_requests: list = field(default_factory=list)  # requests whose chunks fill the arena, in order
 
 
 def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_tokens: int = 0,
@@ -54,6 +55,7 @@ def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_to
     work: list[list[int]] = []
     dec: list[list[int]] = []
     parts: list = []
+    part_reqs: list[int] = []
     arena = 0
     stats = {"requests": len(lens), "prefill_rows": 0, "decode_rows": 0, "peer_requests": 0}
     for r, tk in enumerate(lens):
@@ -71,6 +73,7 @@ def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_to
             peer_end = min(peer_len, tk)
             peer_off = arena
             parts.extend(chunks)
+            part_reqs.append(r)
             arena += peer_len
             stats["peer_requests"] += 1
         elif split_tokens > 0:
@@ -102,6 +105,7 @@ def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_to
         peer_parts=parts,
         peer_rows=arena,
         stats=stats,
+        part_requests=part_reqs,
     )
 
 

@@ -58,9 +58,13 @@ def test_backend_forward_matches_reference_forward():
     q = t16(z["query"])
     out = torch.zeros(ntok + 8, h, d, dtype=torch.bfloat16, device=dev)  # padded like vLLM
     impl.forward(layer, q, None, None, t16(z["cache"]), meta, out)
+    # a second layer call of the same step reuses the step's plan
+    out2 = torch.zeros_like(out)
+    impl.forward(layer, q, None, None, t16(z["cache"]), meta, out2)
     torch.cuda.synchronize()
     rb.clear_peer_kv()
-    assert rb.IMPL_STATS["attn_cuda"] == 1 and rb.IMPL_STATS["decode_cuda"] == 1
+    assert len(meta._hcp_plans) == 1 and torch.equal(out, out2)
+    assert rb.IMPL_STATS["attn_cuda"] == 2 and rb.IMPL_STATS["decode_cuda"] == 2
     got = out[:ntok].float().cpu().numpy()
     want = ro.bf16_bits_to_f32(z["output"])
     err = np.abs(got - want)
@@ -124,10 +128,12 @@ def test_backend_split_tokens_matches_oracle(monkeypatch):
         seq_lens=torch.tensor([tk for _, tk in reqs], dtype=torch.int32, device=dev),
         block_table=torch.from_numpy(bt).to(dev))
     out = torch.zeros(int(qsl[-1]), h, d, dtype=torch.bfloat16, device=dev)
-    impl.forward(types.SimpleNamespace(layer_name="model.layers.0.self_attn.attn"), t16(query), None, None,
-                 t16(cache), meta, out)
+    for i in range(2):  # two layers of one step: the second reuses the plan
+        impl.forward(types.SimpleNamespace(layer_name=f"model.layers.{i}.self_attn.attn"), t16(query), None,
+                     None, t16(cache), meta, out)
     torch.cuda.synchronize()
-    assert rb.IMPL_STATS["attn_cuda"] == 1 and rb.IMPL_STATS["decode_cuda"] == 1
+    assert len(meta._hcp_plans) == 1
+    assert rb.IMPL_STATS["attn_cuda"] == 2 and rb.IMPL_STATS["decode_cuda"] == 2
     got = out.float().cpu().numpy()
     err = np.abs(got - want)
     assert (err <= 2e-3 + 2.0 ** -7 * np.abs(want)).all(), f"max err {err.max():.3e}"
