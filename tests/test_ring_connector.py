@@ -312,3 +312,82 @@ def test_chunk_transport_nvlink_two_gpus(tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     _cross_process(tmp_path, 0, 1)
+
+
+@pytest.mark.gpu
+def test_connector_staging_feeds_backend_forward(tmp_path):
+    """The reference's data flow on this package: two producers save chunks
+    c0, c1 from their paged caches; a consumer connector stages them for a
+    request (prefix [c0, c1]); the CUSTOM backend's forward, layer by layer
+    after wait_for_layer_load, reads the staged chunks as the non-causal
+    peer prefix and the request's own keys from its cache.  Compared with
+    the oracle's restatement of the reference forward with the same staged
+    prefix (tolerance 2e-3 + 2^-7 |ref|)."""
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+    import types
+    from hcp_vllm_plugin_b200 import ring_backend as rb
+    from hcp_vllm_plugin_b200.ring_connector import HcpRingConnectorMetadata, HcpRingKvConnector, RingReqMeta
+
+    dev = torch.device("cuda:0")
+    shared = str(tmp_path)
+    layers, h = 2, 28
+    names = [f"model.layers.{i}.self_attn.attn" for i in range(layers)]
+    g = torch.Generator().manual_seed(21)
+
+    def rnd(*shape):
+        return torch.randn(*shape, generator=g).to(torch.bfloat16)
+
+    # producers: chunk c0 (64 tokens), c1 (48 tokens) out of their own pools
+    chunk_blocks = {"c0": [3, 7, 1, 9], "c1": [2, 5, 8]}
+    prod_caches = {ck: [rnd(12, HKV, BS, 2 * D) for _ in range(layers)] for ck in chunk_blocks}
+    producers = []
+    for ck, blocks in chunk_blocks.items():
+        prod = HcpRingKvConnector(_config(dict(ring_role="producer", ring_shared_path=shared, ring_run_id="run",
+                                               ring_chunk_id=ck), layers=layers), KVConnectorRole.WORKER)
+        sm = (torch.tensor(blocks)[:, None] * BS + torch.arange(BS)[None, :]).flatten()
+        prod.bind_connector_metadata(HcpRingConnectorMetadata(
+            requests=[RingReqMeta(is_store=True, chunk_key=ck, slot_mapping=sm)]))
+        for i, n in enumerate(names):
+            prod.save_kv_layer(n, prod_caches[ck][i].to(dev), None)
+        prod.wait_for_save()
+        producers.append(prod)
+    prefix = sum(len(b) * BS for b in chunk_blocks.values())          # 112 tokens
+    # consumer: one request with 40 new tokens after the prefix
+    tq = 40
+    tk = prefix + tq
+    nbl = (tk + BS - 1) // BS
+    bt = torch.tensor([[30 + i for i in range(nbl)]], dtype=torch.int32)
+    cons_caches = [rnd(30 + nbl, HKV, BS, 2 * D) for _ in range(layers)]
+    queries = [rnd(tq, h, D) for _ in range(layers)]
+    cons = HcpRingKvConnector(_config(dict(ring_role="consumer", ring_shared_path=shared, ring_run_id="run",
+                                           ring_prefix_chunk_ids="c0,c1", ring_prefix_len=prefix), layers=layers),
+                              KVConnectorRole.WORKER)
+    cons.bind_connector_metadata(_load_meta([("r0", int(bt[0, 0]), ["c0", "c1"], prefix)]))
+    dev_caches = {n: c.to(dev) for n, c in zip(names, cons_caches)}
+    cons.start_load_kv(fk.forward_context(dev_caches))
+    impl = rb.HcpRingAttentionImpl(h, D, D ** -0.5, HKV)
+    meta = types.SimpleNamespace(num_actual_tokens=tq, query_start_loc=torch.tensor([0, tq], dtype=torch.int32, device=dev),
+                                 seq_lens=torch.tensor([tk], dtype=torch.int32, device=dev), block_table=bt.to(dev))
+    for i, n in enumerate(names):
+        cons.wait_for_layer_load(n)
+        out = torch.zeros(tq, h, D, dtype=torch.bfloat16, device=dev)
+        impl.forward(types.SimpleNamespace(layer_name=n), queries[i].to(dev), None, None, dev_caches[n], meta, out)
+        torch.cuda.synchronize()
+        # oracle: the same staged prefix (chunks gathered from the producers' pools)
+        kp, vp = [], []
+        for ck, blocks in chunk_blocks.items():
+            sm = (np.array(blocks)[:, None] * BS + np.arange(BS)[None, :]).reshape(-1)
+            k, v = orc.kv_cache_gather(prod_caches[ck][i].float().numpy(), sm)
+            kp.append(k)
+            vp.append(v)
+        batch = orc.RingBatch(query=queries[i].float().numpy(), cache=cons_caches[i].float().numpy(),
+                              block_table=bt.numpy(), query_start_loc=np.array([0, tq]), seq_lens=np.array([tk]),
+                              scale=D ** -0.5, staged={0: (np.concatenate(kp), np.concatenate(vp))})
+        want = orc.ring_forward(batch)
+        err = np.abs(out.float().cpu().numpy() - want)
+        assert np.all(err <= 2e-3 + 2.0 ** -7 * np.abs(want)), (n, float(err.max()))
+    cons.get_finished({"r0"})
+    assert rb.PEER_KV_STAGING == {} and rb.PEER_REQ_MAP == {}
+    cons.shutdown()
+    for prod in producers:
+        prod.shutdown()
