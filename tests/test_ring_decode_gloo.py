@@ -105,7 +105,7 @@ def test_ring_decode_single_rank():
     assert worst < 1e-5 and growth_ok
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 8])
 def test_ring_decode_gloo(world):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
