@@ -551,7 +551,8 @@ def run_rows(args, world, rank, local_rank):
             res["f3_merge_n"] = {"error": repr(e)}
 
     # f3: ring decode over all ranks
-    B, total, warm, steps = 64, 65536, 3, 10
+    # every rank receives a decode token within the first N warm-up steps
+    B, total, warm, steps = 64, 65536, max(3, world), 10
     chunk = total // world
     rd = RingDecode(1, B, chunk + warm + steps + 1, H, HKV, D, D ** -0.5, dev)
     for b in range(B):

@@ -92,6 +92,11 @@ class RingDecode:
         self.policy = growth_policy
         self.k = torch.zeros(num_layers, batch * capacity, num_kv_heads, head_dim, dtype=dtype, device=device)
         self.v = torch.zeros_like(self.k)
+        # Run the growth append's index kernels once now (row 0 onto itself):
+        # a rank that launches them for the first time inside a step loads
+        # their module there, and every rank's next collective waits for it.
+        idx = torch.zeros(1, dtype=torch.long, device=device)
+        self.k[0].index_copy_(0, idx, self.k[0].index_select(0, idx))
         self.lens = [[0] * batch for _ in range(num_layers)]
         self.growth_positions = [[[] for _ in range(batch)] for _ in range(num_layers)]
         h, d, hkv = num_heads, head_dim, num_kv_heads
