@@ -44,7 +44,10 @@ logger = init_logger(__name__)
 # Peer KV staging (module level), same contract as the reference
 # (ring_backend.py:92-136): the connector writes, forward() reads.
 # Keyed by (chunk_key, layer_name); a request is bound to its ORDERED prefix
-# chunk keys by its first block-table block id.
+# chunk keys by its first block-table block id.  Connector threads insert
+# while the worker thread reads and deletes, so every scan below iterates a
+# snapshot (``list(dict)`` copies the keys without running Python code, so no
+# other thread can change the dict in between).
 # ---------------------------------------------------------------------------
 PEER_KV_STAGING: dict[tuple[str, str], tuple[torch.Tensor, torch.Tensor]] = {}
 PEER_REQ_MAP: dict[int, list[str]] = {}
@@ -59,16 +62,14 @@ def stage_peer_kv(chunk_key: str, layer_name: str, k: torch.Tensor, v: torch.Ten
     """Stage one peer chunk's K/V ([T, Hkv, D], K post-RoPE) for one layer."""
     PEER_KV_STAGING[(chunk_key, layer_name)] = (k, v)
     STAGING_STATS["max_staged_layers"] = max(STAGING_STATS["max_staged_layers"], len(PEER_KV_STAGING))
-    chunks = {key[0] for key in PEER_KV_STAGING}
+    chunks = {key[0] for key in list(PEER_KV_STAGING)}
     STAGING_STATS["max_concurrent_chunks"] = max(STAGING_STATS["max_concurrent_chunks"], len(chunks))
     STAGING_STATS["last_chunk_len"] = int(k.shape[0])
 
 
 def drop_chunk_kv(chunk_key: str) -> int:
-    keys = [key for key in PEER_KV_STAGING if key[0] == chunk_key]
-    for key in keys:
-        del PEER_KV_STAGING[key]
-    return len(keys)
+    keys = [key for key in list(PEER_KV_STAGING) if key[0] == chunk_key]
+    return sum(PEER_KV_STAGING.pop(key, None) is not None for key in keys)
 
 
 def map_request_peer(first_block_id: int, chunk_keys) -> None:
@@ -214,7 +215,7 @@ class HcpRingAttentionImpl(AttentionImpl):
             ck_list = PEER_REQ_MAP.get(int(bt0[r]))
             if ck_list is None and len(seq_lens) == 1:
                 # single-request fallback, as the reference (ring_backend.py:746-755)
-                chunks = {key[0] for key in PEER_KV_STAGING}
+                chunks = {key[0] for key in list(PEER_KV_STAGING)}
                 if len(chunks) == 1:
                     ck_list = [next(iter(chunks))]
             if not ck_list:

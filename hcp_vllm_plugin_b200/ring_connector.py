@@ -271,7 +271,7 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         self._stage_lock = threading.Lock()
         self._side_stream = None
         self._stores: dict[str, torch.Tensor] = {}       # producer: chunk -> [L, 2, T, Hkv, D]
-        self._store_slots: dict[str, torch.Tensor] = {}  # producer: chunk -> device slot mapping
+        self._store_slots: dict[str, tuple] = {}         # producer: chunk -> (host, device) slots
         self._saved_layers: dict[str, set[int]] = {}
         os.makedirs(self._run_dir(), exist_ok=True)
 
@@ -464,8 +464,9 @@ class HcpRingKvConnector(KVConnectorBase_V1):
                         kv[1].record_stream(cur)
             st.consumed_idx = max(st.consumed_idx, idx)
         # transient staging of layers already consumed goes away
-        for key in [key for key in PEER_KV_STAGING if layer_index(key[1]) < idx]:
-            del PEER_KV_STAGING[key]
+        with self._stage_lock:
+            for key in [key for key in list(PEER_KV_STAGING) if layer_index(key[1]) < idx]:
+                PEER_KV_STAGING.pop(key, None)
 
     # ------------------------------------------------------------------ worker side: save
     def save_kv_layer(self, layer_name: str, kv_layer: torch.Tensor, attn_metadata: Any,
@@ -486,11 +487,14 @@ class HcpRingKvConnector(KVConnectorBase_V1):
                 self._stores[req.chunk_key] = store
                 _LOCAL_EXPORTS[(self._run_id, req.chunk_key)] = store
                 self._saved_layers[req.chunk_key] = set()
-            slots = self._store_slots.get(req.chunk_key)
-            if slots is None or slots.shape[0] != n:
-                slots = req.slot_mapping.to(kv_layer.device)
-                self._store_slots[req.chunk_key] = slots
-            ops.kv_cache_gather(kv_layer, slots, key=store[idx, 0], value=store[idx, 1])
+            # one device copy of this request's slots for all its layers (keyed
+            # by the host tensor itself: another request saving the same chunk
+            # key from other blocks must not reuse it)
+            cached = self._store_slots.get(req.chunk_key)
+            if cached is None or cached[0] is not req.slot_mapping:
+                cached = (req.slot_mapping, req.slot_mapping.to(kv_layer.device))
+                self._store_slots[req.chunk_key] = cached
+            ops.kv_cache_gather(kv_layer, cached[1], key=store[idx, 0], value=store[idx, 1])
             self._saved_layers[req.chunk_key].add(idx)
 
     def wait_for_save(self) -> None:

@@ -188,6 +188,38 @@ def test_streaming_window_and_refcounts(tmp_path, monkeypatch, window):
     assert rb.PEER_REQ_MAP == {} and rb.PEER_KV_STAGING == {}
 
 
+def test_producer_resave_reads_the_new_requests_blocks(tmp_path, monkeypatch):
+    """Two requests save the same chunk key, equal length, different blocks:
+    the second save must gather from the second request's blocks (the device
+    gather is replaced by a CPU restatement of the pool -> chunk copy)."""
+    from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
+    from hcp_vllm_plugin_b200 import ring_connector as rc
+
+    def cpu_gather(cache, slots, key, value):
+        blk, off = slots // BS, slots % BS
+        rows = cache[blk, :, off]                       # [n, Hkv, 2D]
+        key.copy_(rows[..., :D])
+        value.copy_(rows[..., D:])
+
+    monkeypatch.setattr(rc.ops, "kv_cache_gather", cpu_gather)
+    caches = _cache(21, "cpu")
+    prod = rc.HcpRingKvConnector(_config(dict(ring_role="producer", ring_shared_path=str(tmp_path),
+                                              ring_run_id="run", ring_chunk_id="c0")), KVConnectorRole.WORKER)
+    for blocks in (CHUNK_BLOCKS, [b + 1 for b in CHUNK_BLOCKS]):
+        sm = (torch.tensor(blocks)[:, None] * BS + torch.arange(BS)[None, :]).flatten()
+        prod.bind_connector_metadata(rc.HcpRingConnectorMetadata(
+            requests=[rc.RingReqMeta(is_store=True, chunk_key="c0", slot_mapping=sm)]))
+        for i, c in enumerate(caches):
+            prod.save_kv_layer(f"model.layers.{i}.self_attn.attn", c, None)
+        store = prod._stores["c0"]
+        np_sm = sm.numpy()
+        for i, c in enumerate(caches):
+            want_k, want_v = orc.kv_cache_gather(c.view(torch.int16).numpy().view(np.uint16), np_sm)
+            np.testing.assert_array_equal(store[i, 0].view(torch.int16).numpy().view(np.uint16), want_k)
+            np.testing.assert_array_equal(store[i, 1].view(torch.int16).numpy().view(np.uint16), want_v)
+    prod.shutdown()
+
+
 def test_missing_chunk_raises(tmp_path):
     STORES.clear()
     conn = _consumer(str(tmp_path), 2)
