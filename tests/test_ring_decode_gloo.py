@@ -22,17 +22,17 @@ H, HKV, D, LAYERS, STEPS = 4, 2, 16, 2, 7
 CHUNKS = (8, 12, 5)  # per-rank prefix rows of each request
 
 
-def _cpu_partial(q, kv_k, kv_v, lens, cap, *, scale, num_kv_heads, out, lse):
-    for b, n in enumerate(lens):
+def _cpu_partial(q, kv_k, kv_v, segs, *, scale, num_kv_heads, out, lse):
+    for i, start, n in segs:
         if n == 0:
-            out[b] = 0
-            lse[:, b] = float("-inf")
+            out[i] = 0
+            lse[:, i] = float("-inf")
             continue
-        rows = slice(b * cap, b * cap + n)
-        o, l = ro.attn_with_lse(q[b:b + 1].float().numpy(), kv_k[rows].float().numpy(),
+        rows = slice(start, start + n)
+        o, l = ro.attn_with_lse(q[i:i + 1].float().numpy(), kv_k[rows].float().numpy(),
                                 kv_v[rows].float().numpy(), scale, None)
-        out[b] = torch.from_numpy(o[0])
-        lse[:, b] = torch.from_numpy(l[:, 0])
+        out[i] = torch.from_numpy(o[0])
+        lse[:, i] = torch.from_numpy(l[:, 0])
 
 
 def _cpu_merge(out, states_o, states_lse, out_lse):
@@ -52,10 +52,20 @@ def _data(world):
     return ks, vs, qs
 
 
-def _run(rank, world, result_q=None):
+def cpu_ring_decode():
+    """RingDecode with the CPU checkers as its device ops (a subclass, so the
+    product class is left as it is for other tests in the same process)."""
     from hcp_vllm_plugin_b200.ring_decode import RingDecode
-    RingDecode.partial_fn = staticmethod(_cpu_partial)
-    RingDecode.merge_fn = staticmethod(_cpu_merge)
+
+    class CpuRingDecode(RingDecode):
+        partial_fn = staticmethod(_cpu_partial)
+        merge_fn = staticmethod(_cpu_merge)
+
+    return CpuRingDecode
+
+
+def _run(rank, world, result_q=None):
+    RingDecode = cpu_ring_decode()
     ks, vs, qs = _data(world)
     B = len(CHUNKS)
     cap = max(CHUNKS) + STEPS
