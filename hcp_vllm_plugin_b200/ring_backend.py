@@ -25,6 +25,7 @@ path: every op runs in ``libhcp_ring.so`` and raises if it is missing.
 from __future__ import annotations
 
 import os
+import re
 
 import torch
 
@@ -39,6 +40,7 @@ from . import ops
 from .ring_plan import misaligned_paged_starts, plan_layer
 
 logger = init_logger(__name__)
+_LAYER_RE = re.compile(r"layers\.(\d+)\.")
 
 # ---------------------------------------------------------------------------
 # Peer KV staging (module level), same contract as the reference
@@ -55,7 +57,8 @@ PEER_REQ_MAP: dict[int, list[str]] = {}
 STAGING_STATS: dict = {"max_concurrent_chunks": 0, "max_staged_layers": 0, "last_chunk_len": 0}
 BATCH_STATS: dict = {"max_reqs": 0}
 # Which device paths ran (validation evidence, as the reference's IMPL_STATS).
-IMPL_STATS: dict = {"attn_cuda": 0, "decode_cuda": 0, "cache_update_cuda": 0, "peer_concat": 0}
+IMPL_STATS: dict = {"attn_cuda": 0, "decode_cuda": 0, "cache_update_cuda": 0, "peer_concat": 0,
+                    "decode_ring": 0}
 
 
 def stage_peer_kv(chunk_key: str, layer_name: str, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -102,6 +105,37 @@ def reset_batch_stats() -> None:
 def reset_impl_stats() -> None:
     for key in IMPL_STATS:
         IMPL_STATS[key] = 0
+
+
+# ---------------------------------------------------------------------------
+# Memory-split decode (the decode ring), same registry as the reference
+# (ring_backend.py:153-211): the connector registers a request by its first
+# block id; its single-token decode rows then run on the ring
+# (``ring_decode.RingDecode``) instead of the local plan.  Entry: ``ring``
+# (the owner's RingDecode), ``slot`` (the request's arena slot),
+# ``prefix_len`` (tokens held by the peers), ``own_len`` (this instance's
+# chunk: set at the first decode step, as the reference does at :648-650),
+# ``installed`` (layers whose own chunk is in the slot already).
+# ---------------------------------------------------------------------------
+DECODE_RING_MAP: dict[int, dict] = {}
+
+
+def _decode_ring_enabled() -> bool:
+    return os.environ.get("HCP_RING_DECODE_RING", "1") == "1"
+
+
+def register_decode_ring(first_block_id: int, ring, slot: int, prefix_len: int) -> None:
+    DECODE_RING_MAP[first_block_id] = {"ring": ring, "slot": int(slot), "prefix_len": int(prefix_len),
+                                       "own_len": None, "installed": set()}
+
+
+def clear_decode_ring(first_block_id: int) -> None:
+    DECODE_RING_MAP.pop(first_block_id, None)
+
+
+def layer_index(layer_name: str) -> int:
+    m = _LAYER_RE.search(layer_name)
+    return int(m.group(1)) if m else 0
 
 
 def _ring_enabled() -> bool:
@@ -207,11 +241,13 @@ class HcpRingAttentionImpl(AttentionImpl):
             pass
         return cached
 
-    def _peers_for_layer(self, layer_name: str, seq_lens, bt0) -> dict:
+    def _peers_for_layer(self, layer_name: str, seq_lens, bt0, skip=frozenset()) -> dict:
         peers: dict[int, list] = {}
         if not _ring_enabled():
             return peers
         for r in range(len(seq_lens)):
+            if r in skip:
+                continue
             ck_list = PEER_REQ_MAP.get(int(bt0[r]))
             if ck_list is None and len(seq_lens) == 1:
                 # single-request fallback, as the reference (ring_backend.py:746-755)
@@ -249,13 +285,16 @@ class HcpRingAttentionImpl(AttentionImpl):
         qsl, seq_lens, bt0 = self._host_meta(attn_metadata)
         BATCH_STATS["max_reqs"] = max(BATCH_STATS["max_reqs"], len(seq_lens))
         layer_name = getattr(layer, "layer_name", "")
-        peers = self._peers_for_layer(layer_name, seq_lens, bt0) if (PEER_REQ_MAP or PEER_KV_STAGING) else {}
+        ring_rows = self._decode_ring_rows(qsl, bt0) if (DECODE_RING_MAP and _decode_ring_enabled()) else []
+        excluded = frozenset(r for r, _ in ring_rows)
+        peers = self._peers_for_layer(layer_name, seq_lens, bt0, excluded) \
+            if (PEER_REQ_MAP or PEER_KV_STAGING) else {}
         block_size = kv_cache.shape[2]
         split = _split_tokens() if _ring_enabled() else 0
         # The plan depends on lengths only (requests, staged chunks), which
         # every layer of a step shares: build it once per step and rebuild
         # just this layer's list of staged tensors.
-        sig = (block_size, split,
+        sig = (block_size, split, excluded,
                tuple((r, tuple(int(k.shape[0]) for k, _ in ch)) for r, ch in sorted(peers.items())))
         plans = getattr(attn_metadata, "_hcp_plans", None)
         if plans is None:
@@ -266,7 +305,7 @@ class HcpRingAttentionImpl(AttentionImpl):
                 pass
         plan = plans.get(sig)
         if plan is None:
-            plan = plan_layer(qsl, seq_lens, block_size, peers, split)
+            plan = plan_layer(qsl, seq_lens, block_size, peers, split, exclude=excluded)
             if misaligned_paged_starts(plan, block_size):
                 raise ValueError("HCP ring backend: peer prefix length must be a multiple of the block size")
             plans[sig] = plan
@@ -292,4 +331,74 @@ class HcpRingAttentionImpl(AttentionImpl):
                                out=out, peer_k=k_a, peer_v=v_a, kv_cache=kv_cache,
                                block_table=block_table)
             IMPL_STATS["decode_cuda"] += 1
+        if ring_rows:
+            self._decode_ring_forward(layer_index(layer_name), ring_rows, qsl, seq_lens, q, key, value,
+                                      kv_cache, block_table, out)
         return output
+
+    # -- memory-split decode -------------------------------------------------
+    @staticmethod
+    def _decode_ring_rows(qsl, bt0) -> list:
+        """(request index, registry entry) of this step's decode-ring rows:
+        single-token steps of registered requests (``ring_backend.py:639-640``)."""
+        rows = []
+        for r in range(len(qsl) - 1):
+            if qsl[r + 1] - qsl[r] != 1:
+                continue
+            e = DECODE_RING_MAP.get(int(bt0[r]))
+            if e is not None:
+                rows.append((r, e))
+        return rows
+
+    def _decode_ring_forward(self, li: int, ring_rows, qsl, seq_lens, q, key, value, kv_cache,
+                             block_table, out) -> None:
+        """The owner's side of one layer of the decode ring for this step's
+        ring rows (the reference's per-request local partial + packet,
+        ``ring_backend.py:641-729``, here one collective step per ring).
+
+        At a request's first decode step every layer first moves the
+        request's own chunk (positions ``[prefix_len, prefix_len + own_len)``
+        of its paged cache) into its ring slot, once; the reference rebuilds
+        that segment by concatenation at every step."""
+        by_ring: dict[int, tuple] = {}
+        for r, e in ring_rows:
+            by_ring.setdefault(id(e["ring"]), (e["ring"], []))[1].append((r, e))
+        for ring, rows in by_ring.values():
+            if abs(ring.scale - self.scale) > 1e-6 * self.scale:
+                raise ValueError(f"HCP decode ring: ring scale {ring.scale} != layer scale {self.scale}")
+            slots, positions, fresh = [], [], []
+            for r, e in rows:
+                tk = int(seq_lens[r])
+                if e["own_len"] is None:
+                    e["own_len"] = tk - 1 - e["prefix_len"]  # tk counts the current token
+                if not e["installed"]:
+                    fresh.append(e["slot"])
+                slots.append(e["slot"])
+                positions.append(tk - 1)
+            if li == 0:
+                ring.begin_step(slots, positions, fresh)
+            for r, e in rows:
+                if li not in e["installed"]:
+                    self._install_own_chunk(ring, li, r, e, kv_cache, block_table)
+                    e["installed"].add(li)
+            idx = torch.tensor([qsl[r] for r, _ in rows], dtype=torch.long)
+            if q.is_cuda:
+                idx = idx.pin_memory().to(q.device, non_blocking=True)
+            res = torch.empty(len(rows), q.shape[1], q.shape[2], dtype=out.dtype, device=out.device)
+            ring.step(li, positions, q.index_select(0, idx), key.index_select(0, idx),
+                      value.index_select(0, idx), res, slots=slots)
+            out.index_copy_(0, idx, res)
+            IMPL_STATS["decode_ring"] += 1
+
+    @staticmethod
+    def _install_own_chunk(ring, li, r, e, kv_cache, block_table) -> None:
+        n, start = e["own_len"], e["prefix_len"]
+        kk, vv = ring.install_rows(li, e["slot"], n)
+        if n <= 0:
+            return
+        bs = kv_cache.shape[2]
+        blocks = block_table[r, start // bs:(start + n + bs - 1) // bs].to(torch.int64)
+        offs = torch.arange(bs, dtype=torch.int64, device=blocks.device)
+        lead = start % bs
+        slots = (blocks[:, None] * bs + offs[None, :]).flatten()[lead:lead + n].contiguous()
+        ops.kv_cache_gather(kv_cache, slots, key=kk, value=vv)

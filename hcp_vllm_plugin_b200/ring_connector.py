@@ -58,13 +58,16 @@ from vllm.distributed.kv_transfer.kv_connector.v1.base import (
     KVConnectorMetadata,
     KVConnectorRole,
 )
+from vllm.logger import init_logger
 
 from . import _capi as C
 from . import ops
 from .ring_backend import (
     PEER_KV_STAGING,
+    clear_decode_ring,
     drop_chunk_kv,
     map_request_peer,
+    register_decode_ring,
     stage_peer_kv,
     unmap_request_peer,
 )
@@ -77,8 +80,15 @@ if TYPE_CHECKING:
     from vllm.v1.kv_cache_interface import KVCacheConfig
     from vllm.v1.request import Request
 
+logger = init_logger(__name__)
 _LAYER_RE = re.compile(r"layers\.(\d+)\.")
 _DTYPES = {"bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def decode_ring_on() -> bool:
+    """``HCP_RING_DECODE_RING`` (default on, as the reference's
+    ``ring_connector.py:129-134``); the ring also needs ``ring_decode_addr``."""
+    return os.environ.get("HCP_RING_DECODE_RING", "1") == "1"
 
 
 def stream_window() -> int:
@@ -260,6 +270,35 @@ class HcpRingKvConnector(KVConnectorBase_V1):
                 self._prefix_chunk_ids = ids[:i]
                 self._prefix_peer_urls = [urls[i - 1] if i > 0 else ""] * i
         self._poll_interval = float(cfg.get_from_extra_config("ring_ready_poll_interval_s", 0.5))
+        # Memory-split decode (the decode ring): the nodes of ring_order form
+        # their own process group, rendezvous at ring_decode_addr
+        # ("host:port", hosted by rank 0); a node's rank is its chunk's index
+        # in ring_order, so the owner (the last chunk) is rank N-1 and the
+        # peers are 0..N-2 in prefix order, as the reference's growth indexing
+        # (ring_decode.py:30-43).  Peers serve their chunk store; the owner
+        # sends its decode rows through the ring (ring_backend).
+        order_ids = [x.split("@")[0] for x in as_str_list(order)]
+        self._decode_addr = str(cfg.get_from_extra_config("ring_decode_addr", "") or "")
+        self._decode_rank = int(cfg.get_from_extra_config(
+            "ring_decode_index", order_ids.index(self._chunk_id) if self._chunk_id in order_ids else -1))
+        self._decode_world = int(cfg.get_from_extra_config("ring_decode_world", len(order_ids)))
+        self._decode_slots = int(cfg.get_from_extra_config("ring_decode_slots", 4))
+        self._decode_capacity = int(cfg.get_from_extra_config("ring_decode_capacity", 17408))
+        self._decode_backend = str(cfg.get_from_extra_config("ring_decode_backend", "nccl"))
+        self._decode_on = bool(self._decode_addr) and decode_ring_on() and \
+            0 <= self._decode_rank < self._decode_world
+        self._decode_owner = self._decode_on and self._decode_rank == self._decode_world - 1
+        # With the decode ring, staged prefix KV of a consumed layer is freed
+        # at once (memory-split); without it, decode steps read the staged
+        # prefix again, so it stays until the request finishes (the
+        # reference's bulk staging when the decode ring is off).
+        self._drop_consumed = self._decode_on
+        self._decode_ring = None
+        self._decode_free_slots = list(range(self._decode_slots))
+        self._decode_slot_of: dict[str, int] = {}
+        self._decode_stop = threading.Event()
+        self._decode_thread: threading.Thread | None = None
+        self._decode_error: BaseException | None = None
         self._ready_ok: set[str] = set()
         self._ready_next_poll: dict[str, float] = {}
         self._requests_need_load: dict[str, Any] = {}
@@ -274,6 +313,63 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         self._store_slots: dict[str, tuple] = {}         # producer: chunk -> (host, device) slots
         self._saved_layers: dict[str, set[int]] = {}
         os.makedirs(self._run_dir(), exist_ok=True)
+        if self._decode_on and not self._decode_owner and self._role == KVConnectorRole.WORKER:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
+                else torch.device("cpu")
+            self._decode_thread = threading.Thread(target=self._serve_decode_ring, args=(device,), daemon=True)
+            self._decode_thread.start()
+
+    # ------------------------------------------------------------------ decode ring
+    def _make_decode_ring(self, device: torch.device):
+        """Join the decode ring's group (returns once all N nodes joined) and
+        build this node's ring state."""
+        from .ring_decode import RingComm, RingDecode
+
+        host, port = self._decode_addr.rsplit(":", 1)
+        comm = RingComm.standalone(host, int(port), self._decode_rank, self._decode_world,
+                                   backend=self._decode_backend)
+        hf = self._vllm_config.model_config.hf_config
+        h, hkv = hf.num_attention_heads, hf.num_key_value_heads
+        d = getattr(hf, "head_dim", None) or hf.hidden_size // h
+        return RingDecode(self._num_layers, self._decode_slots, self._decode_capacity, h, hkv, d, d ** -0.5,
+                          device, dtype=self._vllm_config.model_config.dtype, comm=comm,
+                          growth_policy=os.environ.get("HCP_RING_DECODE_GROWTH", "rr"))
+
+    def _decode_chunk(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """This node's chunk for ``layer``, out of its chunk store (the
+        reference's node serves its own chunk snapshot,
+        ``ring_decode.py:246-249``)."""
+        store = self._stores.get(self._chunk_id)
+        if store is None:
+            raise RuntimeError(f"HcpRingKvConnector: decode ring peer has no saved chunk {self._chunk_id}")
+        return store[layer, 0], store[layer, 1]
+
+    def _serve_decode_ring(self, device: torch.device) -> None:
+        """Peer nodes: the ring's serve loop in a thread of the worker, on
+        its own stream (the reference's relay thread, ``ring_decode.py:284-318``)."""
+        try:
+            if device.type == "cuda":
+                torch.cuda.set_device(device)
+            ring = self._make_decode_ring(device)
+            self._decode_ring = ring
+            if device.type == "cuda":
+                with torch.cuda.stream(torch.cuda.Stream(device=device)):
+                    ring.serve(self._decode_chunk, stop=self._decode_stop)
+            else:
+                ring.serve(self._decode_chunk, stop=self._decode_stop)
+        except BaseException as e:  # noqa: BLE001 - a dead peer must not take the worker down
+            self._decode_error = e
+            logger.error("HcpRingKvConnector: decode ring peer %d stopped: %r", self._decode_rank, e)
+
+    def _register_decode(self, req: "RingReqMeta", expected: int, device: torch.device) -> None:
+        if self._decode_ring is None:
+            self._decode_ring = self._make_decode_ring(device)
+        if not self._decode_free_slots:
+            raise RuntimeError(f"HcpRingKvConnector: all {self._decode_slots} decode ring slots are in use "
+                               "(ring_decode_slots)")
+        slot = self._decode_free_slots.pop(0)
+        self._decode_slot_of[req.req_id] = slot
+        register_decode_ring(req.first_block_id, self._decode_ring, slot, expected)
 
     # ------------------------------------------------------------------ paths
     def _run_dir(self) -> str:
@@ -434,6 +530,8 @@ class HcpRingKvConnector(KVConnectorBase_V1):
             self._live[req.req_id] = (req.first_block_id, list(req.chunk_keys))
             for ck in req.chunk_keys:
                 self._chunk_refs[ck] = self._chunk_refs.get(ck, 0) + 1
+            if self._decode_owner:
+                self._register_decode(req, expected, device)
             st = _PrefillStream(req.req_id, layer_order, list(req.chunk_keys), expected)
             self._streams[req.req_id] = st
             st.thread = threading.Thread(target=self._stream_worker, args=(st, device), daemon=True)
@@ -463,6 +561,8 @@ class HcpRingKvConnector(KVConnectorBase_V1):
                         kv[0].record_stream(cur)
                         kv[1].record_stream(cur)
             st.consumed_idx = max(st.consumed_idx, idx)
+        if not self._drop_consumed:
+            return
         # transient staging of layers already consumed goes away
         with self._stage_lock:
             for key in [key for key in list(PEER_KV_STAGING) if layer_index(key[1]) < idx]:
@@ -536,6 +636,10 @@ class HcpRingKvConnector(KVConnectorBase_V1):
             return
         first_block_id, chunk_keys = live
         unmap_request_peer(first_block_id)
+        slot = self._decode_slot_of.pop(req_id, None)
+        if slot is not None:
+            clear_decode_ring(first_block_id)
+            self._decode_free_slots.append(slot)
         for ck in chunk_keys:
             refs = self._chunk_refs.get(ck, 0) - 1
             if refs <= 0:
@@ -555,6 +659,11 @@ class HcpRingKvConnector(KVConnectorBase_V1):
     def shutdown(self) -> None:
         for req_id in list(self._live):
             self._release_live_entry(req_id)
+        if self._decode_owner and self._decode_ring is not None:
+            self._decode_ring.stop()          # ends the peers' serve loops
+        self._decode_stop.set()
+        if self._decode_thread is not None:
+            self._decode_thread.join(timeout=30)
         for ck in list(self._chunk_refs):
             drop_chunk_kv(ck)
         self._chunk_refs.clear()

@@ -42,13 +42,15 @@ class LayerPlan:
 
 
 def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_tokens: int = 0,
-               decode_kernel: bool = True) -> LayerPlan:
+               decode_kernel: bool = True, exclude=frozenset()) -> LayerPlan:
     """Build the plan.
 
     ``peers`` maps a request index to its ordered list of staged ``(k, v)``
     chunk tensors for this layer (``[T, Hkv, D]`` each), or is missing the
     request when it has none.  ``split_tokens`` > 0 splits the paged cache
     itself when no peer KV is staged (the single-process validation mode).
+    Requests in ``exclude`` are computed elsewhere (the decode ring) and get
+    no work here.
     """
     qsl = [int(x) for x in query_start_loc]
     lens = [int(x) for x in seq_lens]
@@ -61,7 +63,7 @@ def plan_layer(query_start_loc, seq_lens, block_size: int, peers: dict, split_to
     for r, tk in enumerate(lens):
         qs, qe = qsl[r], qsl[r + 1]
         tq = qe - qs
-        if tq <= 0:
+        if tq <= 0 or r in exclude:
             continue
         qpos0 = tk - tq
         chunks = peers.get(r)

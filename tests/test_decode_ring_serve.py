@@ -95,7 +95,8 @@ def _rank_body(rank, port):
                        [tok[r][j][layer][1] for j in range(seen[r] + 1)]
                 want, _ = ro.attn_with_lse(q[i:i + 1].numpy(), torch.cat(keys).numpy(),
                                            torch.cat(vals).numpy(), D ** -0.5, None)
-                worst = max(worst, float(np.abs(out[i].numpy() - want[0]).max()))
+                err = float(np.abs(out[i].numpy() - want[0]).max())
+                worst = max(worst, err if np.isfinite(err) else float("inf"))  # NaN must fail
         for r, _, _ in rows:
             seen[r] += 1
     ring.stop()

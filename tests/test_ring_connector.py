@@ -129,15 +129,43 @@ def _layers(n):
     return [f"model.layers.{i}.self_attn.attn" for i in range(n)]
 
 
-def _consumer(shared, layers, extra=None):
+class FakeRing:
+    """Stand-in for the decode ring's state (no process group): records the
+    chunks a peer's serve loop reads."""
+
+    def __init__(self):
+        self.served = None
+        self.stopped = False
+
+    def serve(self, chunk_fn, stop):
+        while not stop.is_set():
+            try:
+                self.served = [chunk_fn(i) for i in range(2)]
+                break
+            except RuntimeError:          # chunk not saved yet
+                stop.wait(0.01)
+        stop.wait(30)
+
+    def stop(self):
+        self.stopped = True
+
+
+# the owner of a 3-node decode ring (config only: the ring itself is faked)
+OWNER = dict(ring_decode_addr="127.0.0.1:1", ring_decode_index=2, ring_decode_world=3)
+
+
+def _consumer(shared, layers, extra=None, role="consumer"):
     from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
     from hcp_vllm_plugin_b200.ring_connector import HcpRingKvConnector
 
-    cfg = dict(ring_role="consumer", ring_shared_path=shared, ring_run_id="run")
+    cfg = dict(ring_role=role, ring_shared_path=shared, ring_run_id="run")
     cfg.update(extra or {})
 
     class CpuConnector(HcpRingKvConnector):
         source_cls = FakeSource
+
+        def _make_decode_ring(self, device):
+            return FakeRing()
 
     return CpuConnector(_config(cfg, layers=layers), KVConnectorRole.WORKER)
 
@@ -152,6 +180,9 @@ def _load_meta(reqs, finished=()):
 
 @pytest.mark.parametrize("window", [1, 2, 3])
 def test_streaming_window_and_refcounts(tmp_path, monkeypatch, window):
+    """Decode-ring owner: memory-split staging (consumed layers freed at once,
+    ``ring_connector.py:861-879``), each request registered for the ring
+    with its own slot, released when it finishes."""
     from hcp_vllm_plugin_b200 import ring_backend as rb
 
     monkeypatch.setenv("HCP_RING_STREAM_WINDOW", str(window))
@@ -162,11 +193,12 @@ def test_streaming_window_and_refcounts(tmp_path, monkeypatch, window):
     STORES["c1"] = torch.randn(nl, 2, 48, 2, 8, generator=g)
     for ck, st in STORES.items():
         _write_marker(str(tmp_path), ck, st)
-    conn = _consumer(str(tmp_path), nl)
+    conn = _consumer(str(tmp_path), nl, OWNER)
     conn.bind_connector_metadata(_load_meta([("r0", 3, ["c0", "c1"], 80), ("r1", 9, ["c0"], 32)]))
     names = _layers(nl)
     conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in names}))
     assert rb.PEER_REQ_MAP == {3: ["c0", "c1"], 9: ["c0"]}
+    assert {fb: (e["slot"], e["prefix_len"]) for fb, e in rb.DECODE_RING_MAP.items()} == {3: (0, 80), 9: (1, 32)}
     for i, name in enumerate(names):
         conn.wait_for_layer_load(name)
         for ck in ("c0", "c1"):
@@ -184,8 +216,55 @@ def test_streaming_window_and_refcounts(tmp_path, monkeypatch, window):
     assert 3 not in rb.PEER_REQ_MAP and 9 in rb.PEER_REQ_MAP
     assert not any(key[0] == "c1" for key in rb.PEER_KV_STAGING)
     assert any(key[0] == "c0" for key in rb.PEER_KV_STAGING)
+    assert list(rb.DECODE_RING_MAP) == [9] and conn._decode_free_slots == [2, 3, 0]
     conn.get_finished({"r1"})
-    assert rb.PEER_REQ_MAP == {} and rb.PEER_KV_STAGING == {}
+    assert rb.PEER_REQ_MAP == {} and rb.PEER_KV_STAGING == {} and rb.DECODE_RING_MAP == {}
+    conn.shutdown()
+    assert conn._decode_ring.stopped            # the owner ends the peers' loops
+
+
+def test_staging_kept_without_decode_ring(tmp_path):
+    """No decode ring: decode steps read the staged prefix again, so it stays
+    until the request finishes (the reference's bulk staging)."""
+    from hcp_vllm_plugin_b200 import ring_backend as rb
+
+    nl = 3
+    STORES.clear()
+    STORES["c0"] = torch.randn(nl, 2, 16, 2, 8)
+    _write_marker(str(tmp_path), "c0", STORES["c0"])
+    conn = _consumer(str(tmp_path), nl)
+    conn.bind_connector_metadata(_load_meta([("r0", 5, ["c0"], 16)]))
+    names = _layers(nl)
+    conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in names}))
+    for step in range(2):                       # the prefill step, then a decode step
+        if step:
+            conn.bind_connector_metadata(_load_meta([]))
+            conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in names}))
+        for i, name in enumerate(names):
+            conn.wait_for_layer_load(name)
+            torch.testing.assert_close(rb.PEER_KV_STAGING[("c0", name)][0], STORES["c0"][i, 0], rtol=0, atol=0)
+    assert len(rb.PEER_KV_STAGING) == nl and rb.DECODE_RING_MAP == {}
+    conn.get_finished({"r0"})
+    assert rb.PEER_KV_STAGING == {} and rb.PEER_REQ_MAP == {}
+    conn.shutdown()
+
+
+def test_decode_ring_peer_serves_its_chunk_store(tmp_path):
+    """A peer node (rank 0 of 2) runs the ring's serve loop in a worker
+    thread over its own chunk store; shutdown ends it."""
+    conn = _consumer(str(tmp_path), 2, dict(ring_decode_addr="127.0.0.1:1", ring_decode_index=0,
+                                             ring_decode_world=2, ring_chunk_id="c0"), role="producer")
+    assert conn._decode_thread is not None and not conn._decode_owner
+    store = torch.randn(2, 2, 16, 2, 8)
+    conn._stores["c0"] = store                   # what save_kv_layer builds
+    t0 = time.time()
+    while conn._decode_ring is None or conn._decode_ring.served is None:
+        assert time.time() - t0 < 30
+        time.sleep(0.01)
+    for layer, (k, v) in enumerate(conn._decode_ring.served):
+        assert k.data_ptr() == store[layer, 0].data_ptr() and v.data_ptr() == store[layer, 1].data_ptr()
+    conn.shutdown()
+    assert not conn._decode_thread.is_alive() and conn._decode_error is None
 
 
 def test_producer_resave_reads_the_new_requests_blocks(tmp_path, monkeypatch):
