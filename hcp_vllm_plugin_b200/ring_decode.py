@@ -51,6 +51,7 @@ from . import ops
 
 OP_STOP, OP_STEP = 0, 1
 _HDR = "hcp_decode_ring/hdr/"
+_HDR_KEEP = 64          # step headers kept in the store
 
 
 def growth_assignee(pos: int, ring_size: int, policy: str = "rr") -> int:
@@ -119,6 +120,13 @@ class RingComm:
             raise ValueError(f"unknown backend {backend!r}")
         return cls(pg=pg, store=store)
 
+    def close(self) -> None:
+        """Shut the standalone group down (its communicators and watchdog);
+        a group of the default world belongs to its owner."""
+        if self.pg is not None:
+            self.pg.shutdown()
+            self.pg = None
+
     def _global(self, r: int) -> int:
         return dist.get_global_rank(self.group, r) if self.group is not None else r
 
@@ -149,9 +157,12 @@ class RingComm:
         if self.store is None:
             raise RuntimeError("the decode ring's control plane needs RingComm.standalone")
         self.store.set(f"{_HDR}{seq}", json.dumps(header))
-        if seq >= 2:
-            # every rank read header seq-2 before it joined step seq-1's collectives
-            self.store.delete_key(f"{_HDR}{seq - 2}")
+        if seq >= _HDR_KEEP:
+            # A peer reads header k before it joins step k's collectives, and
+            # the owner's host waits for its GPU at least once per engine step
+            # (vLLM samples every step), which needs step k's collectives
+            # done; so headers this old have been read by every peer.
+            self.store.delete_key(f"{_HDR}{seq - _HDR_KEEP}")
 
     def wait_header(self, seq: int, timeout_s: float) -> dict | None:
         """The owner's header ``seq``, or None if it has not come within

@@ -18,6 +18,7 @@ import socket
 import types
 
 import numpy as np
+import pytest
 import torch
 import torch.multiprocessing as mp
 
@@ -71,6 +72,7 @@ def _body(rank, port):
     peer, own, tok = _data()
     if rank == 0:
         ring.serve(lambda layer: peer[layer], poll_s=0.2)
+        comm.close()
         return {"steps": ring.steps_served}
 
     # owner: paged caches, two requests with their own blocks
@@ -110,6 +112,7 @@ def _body(rank, port):
                 err = float(np.abs(out[r].numpy() - want[0]).max())
                 worst = max(worst, err if np.isfinite(err) else float("inf"))  # NaN must fail
     ring.stop()
+    comm.close()
     for r in range(2):
         rb.clear_decode_ring(int(bt[r, 0]))
     return {"worst": worst, "ring_steps": rb.IMPL_STATS["decode_ring"],
@@ -138,3 +141,115 @@ def test_backend_routes_decode_rows_to_the_ring():
     for r, n in enumerate(OWN):
         pos = [PREFIX + n + t for t in range(STEPS)]
         assert owner["growth"][r] == [p for p in pos if p % 2 == 1]
+
+
+# ---------------------------------------------------------------------------
+# GPU: the same routing on the B200 kernels
+# ---------------------------------------------------------------------------
+def _tol_ok(got, want):
+    err = np.abs(got - want)
+    return bool(np.all(err <= 2e-3 + 2.0 ** -7 * np.abs(want))), float(err.max())
+
+
+@pytest.mark.gpu
+def test_backend_decode_ring_mixed_batch_one_gpu():
+    """One GPU, a one-rank ring (the owner alone, no peer chunk): a batch of
+    a decode-ring request, a plain decode request and a prefill over cached
+    tokens.  The ring request's own chunk moves from the paged cache into its
+    ring slot (``hcp_kv_cache_gather``) at its first decode step, its tokens
+    go to its growth rows, and the other rows run the local plan; every row
+    equals the oracle (2e-3 + 2^-7 |ref|, bf16 output)."""
+    from hcp_vllm_plugin_b200 import ring_backend as rb
+    from hcp_vllm_plugin_b200.ring_decode import RingDecode
+
+    dev = torch.device("cuda:0")
+    h, hkv, d, bs, layers, steps = 28, 4, 128, 16, 2, 3
+    own0, ctx1, cached2, new2 = 200, 300, 96, 64
+    total = [own0 + steps, ctx1 + steps, cached2 + new2]
+    g = torch.Generator().manual_seed(5)
+    K = [[torch.randn(n, hkv, d, generator=g).bfloat16() for n in total] for _ in range(layers)]
+    V = [[torch.randn(n, hkv, d, generator=g).bfloat16() for n in total] for _ in range(layers)]
+    nblk = [(n + bs - 1) // bs for n in total]
+    perm = torch.randperm(sum(nblk), generator=g).to(torch.int32)
+    bt = torch.zeros(3, max(nblk), dtype=torch.int32)
+    o = 0
+    for r, n in enumerate(nblk):
+        bt[r, :n] = perm[o:o + n]
+        o += n
+    caches = []
+    for layer in range(layers):
+        c = torch.zeros(sum(nblk), hkv, bs, 2 * d, dtype=torch.bfloat16)
+        for r, n in enumerate(total):
+            pos = torch.arange(n)
+            blk = bt[r, pos // bs].long()
+            c[blk, :, pos % bs, :d] = K[layer][r]
+            c[blk, :, pos % bs, d:] = V[layer][r]
+        caches.append(c.to(dev))
+    ring = RingDecode(layers, 2, own0 + steps + 1, h, hkv, d, d ** -0.5, dev)
+    rb.DECODE_RING_MAP.clear()
+    rb.reset_impl_stats()
+    rb.register_decode_ring(int(bt[0, 0]), ring, slot=1, prefix_len=0)
+    impl = rb.HcpRingAttentionImpl(h, d, d ** -0.5, hkv)
+    worst = 0.0
+    try:
+        for t in range(steps):
+            reqs = [0, 1, 2] if t == 0 else [0, 1]
+            qlen = {0: 1, 1: 1, 2: new2}
+            seq = {0: own0 + t + 1, 1: ctx1 + t + 1, 2: cached2 + new2}
+            qsl = np.concatenate([[0], np.cumsum([qlen[r] for r in reqs])])
+            meta = types.SimpleNamespace(
+                num_actual_tokens=int(qsl[-1]),
+                query_start_loc=torch.tensor(qsl, dtype=torch.int32, device=dev),
+                seq_lens=torch.tensor([seq[r] for r in reqs], dtype=torch.int32, device=dev),
+                block_table=bt[reqs].to(dev))
+            for layer in range(layers):
+                q = torch.randn(int(qsl[-1]), h, d, generator=g).bfloat16()
+                kn = torch.cat([K[layer][r][seq[r] - qlen[r]:seq[r]] for r in reqs])
+                vn = torch.cat([V[layer][r][seq[r] - qlen[r]:seq[r]] for r in reqs])
+                out = torch.zeros(int(qsl[-1]) + 4, h, d, dtype=torch.bfloat16, device=dev)
+                impl.forward(types.SimpleNamespace(layer_name=f"model.layers.{layer}.self_attn.attn"),
+                             q.to(dev), kn.to(dev), vn.to(dev), caches[layer], meta, out)
+                torch.cuda.synchronize()
+                got = out.float().cpu().numpy()
+                for i, r in enumerate(reqs):
+                    rows = slice(int(qsl[i]), int(qsl[i + 1]))
+                    want, _ = ro.attn_with_lse(q[rows].float().numpy(), K[layer][r][:seq[r]].float().numpy(),
+                                               V[layer][r][:seq[r]].float().numpy(), d ** -0.5,
+                                               seq[r] - qlen[r])
+                    ok, err = _tol_ok(got[rows], want)
+                    assert ok, (t, layer, r, err)
+                    worst = max(worst, err)
+        assert rb.IMPL_STATS["decode_ring"] == steps * layers
+        assert ring.lens[0][1] == own0 + steps          # own chunk + every decode token (one rank)
+    finally:
+        rb.DECODE_RING_MAP.clear()
+
+
+@pytest.mark.gpu
+def test_backend_decode_ring_nccl_two_gpus():
+    """Two GPUs: a peer process serves its chunk on GPU 0 while the owner on
+    GPU 1 runs the backend's forward for two decode-ring requests; the ring
+    is a standalone NCCL group (``decode_ring_backend_worker.py``)."""
+    import os
+    import subprocess
+    import sys
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=os.path.dirname(here))
+    procs = [subprocess.Popen([sys.executable, os.path.join(here, "decode_ring_backend_worker.py"), str(r),
+                               str(port)], env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+             for r in range(2)]
+    outs = []
+    for p in procs:
+        try:
+            outs.append(p.communicate(timeout=400)[0])
+        except subprocess.TimeoutExpired:
+            p.kill()
+            outs.append(p.communicate()[0])
+    assert all(p.returncode == 0 for p in procs), "\n".join(o[-3000:] for o in outs)
+    assert '"ok": true' in outs[1], outs[1][-3000:]
