@@ -55,6 +55,10 @@ PEER_KV_STAGING: dict[tuple[str, str], tuple[torch.Tensor, torch.Tensor]] = {}
 PEER_REQ_MAP: dict[int, list[str]] = {}
 
 STAGING_STATS: dict = {"max_concurrent_chunks": 0, "max_staged_layers": 0, "last_chunk_len": 0}
+# Pool-write evidence (validation only, same keys as the reference's
+# ring_backend.py:255-267): slots written by do_kv_cache_update while
+# enabled, and the decode-ring tokens it skipped.
+WRITE_TRACK: dict = {"enabled": False, "slots": set(), "overlap": 0, "skipped": 0}
 BATCH_STATS: dict = {"max_reqs": 0}
 # Which device paths ran (validation evidence, as the reference's IMPL_STATS).
 IMPL_STATS: dict = {"attn_cuda": 0, "decode_cuda": 0, "cache_update_cuda": 0, "peer_concat": 0,
@@ -100,6 +104,10 @@ def reset_staging_stats() -> None:
 
 def reset_batch_stats() -> None:
     BATCH_STATS["max_reqs"] = 0
+
+
+def reset_write_tracking() -> None:
+    WRITE_TRACK.update(enabled=True, slots=set(), overlap=0, skipped=0)
 
 
 def reset_impl_stats() -> None:
@@ -220,8 +228,37 @@ class HcpRingAttentionImpl(AttentionImpl):
         if n == 0:
             return
         sm = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+        skip = self._decode_ring_skip_rows(layer) if (DECODE_RING_MAP and _decode_ring_enabled()) else []
+        if skip:
+            # Decode-ring tokens are kept by their assignee (memory-split
+            # decode growth): they are not written to this pool
+            # (ring_backend.py:519-531); -1 makes the scatter skip the row.
+            sm = sm.clone()
+            idx = torch.tensor(skip, dtype=torch.long)
+            sm[idx.pin_memory().to(sm.device, non_blocking=True) if sm.is_cuda else idx] = -1
+            WRITE_TRACK["skipped"] += len(skip)
         ops.kv_cache_update(key[:n], value[:n], kv_cache, sm.contiguous())
         IMPL_STATS["cache_update_cuda"] += 1
+        if WRITE_TRACK["enabled"]:
+            WRITE_TRACK["slots"].update(s for s in sm.tolist() if s >= 0)
+
+    def _decode_ring_skip_rows(self, layer) -> list[int]:
+        """Rows of this step's slot mapping that are decode-ring tokens (the
+        single-token step of a registered request), from the step's
+        attention metadata; none when it cannot be attributed."""
+        try:
+            from vllm.forward_context import get_forward_context
+
+            raw = get_forward_context().attn_metadata
+        except Exception:  # noqa: BLE001 - no forward context: skip nothing
+            return []
+        if isinstance(raw, list):
+            raw = raw[0] if raw else None
+        meta = raw.get(getattr(layer, "layer_name", ""), None) if isinstance(raw, dict) else raw
+        if meta is None:
+            return []
+        qsl, _, bt0 = self._host_meta(meta)
+        return [qsl[r] for r, _ in self._decode_ring_rows(qsl, bt0)]
 
     # -- forward -------------------------------------------------------------
     @staticmethod

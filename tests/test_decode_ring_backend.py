@@ -159,6 +159,8 @@ def test_backend_decode_ring_mixed_batch_one_gpu():
     ring slot (``hcp_kv_cache_gather``) at its first decode step, its tokens
     go to its growth rows, and the other rows run the local plan; every row
     equals the oracle (2e-3 + 2^-7 |ref|, bf16 output)."""
+    from vllm.forward_context import override_forward_context
+
     from hcp_vllm_plugin_b200 import ring_backend as rb
     from hcp_vllm_plugin_b200.ring_decode import RingDecode
 
@@ -180,14 +182,16 @@ def test_backend_decode_ring_mixed_batch_one_gpu():
     for layer in range(layers):
         c = torch.zeros(sum(nblk), hkv, bs, 2 * d, dtype=torch.bfloat16)
         for r, n in enumerate(total):
+            n = own0 if r == 0 else n          # the ring request's decode tokens never reach this pool
             pos = torch.arange(n)
             blk = bt[r, pos // bs].long()
-            c[blk, :, pos % bs, :d] = K[layer][r]
-            c[blk, :, pos % bs, d:] = V[layer][r]
+            c[blk, :, pos % bs, :d] = K[layer][r][:n]
+            c[blk, :, pos % bs, d:] = V[layer][r][:n]
         caches.append(c.to(dev))
     ring = RingDecode(layers, 2, own0 + steps + 1, h, hkv, d, d ** -0.5, dev)
     rb.DECODE_RING_MAP.clear()
     rb.reset_impl_stats()
+    rb.reset_write_tracking()
     rb.register_decode_ring(int(bt[0, 0]), ring, slot=1, prefix_len=0)
     impl = rb.HcpRingAttentionImpl(h, d, d ** -0.5, hkv)
     worst = 0.0
@@ -202,13 +206,18 @@ def test_backend_decode_ring_mixed_batch_one_gpu():
                 query_start_loc=torch.tensor(qsl, dtype=torch.int32, device=dev),
                 seq_lens=torch.tensor([seq[r] for r in reqs], dtype=torch.int32, device=dev),
                 block_table=bt[reqs].to(dev))
+            pos = [torch.arange(seq[r] - qlen[r], seq[r]) for r in reqs]
+            slots = torch.cat([bt[r, p // bs].long() * bs + p % bs for r, p in zip(reqs, pos)]).to(dev)
             for layer in range(layers):
+                name = f"model.layers.{layer}.self_attn.attn"
+                lay = types.SimpleNamespace(layer_name=name)
                 q = torch.randn(int(qsl[-1]), h, d, generator=g).bfloat16()
-                kn = torch.cat([K[layer][r][seq[r] - qlen[r]:seq[r]] for r in reqs])
-                vn = torch.cat([V[layer][r][seq[r] - qlen[r]:seq[r]] for r in reqs])
+                kn = torch.cat([K[layer][r][seq[r] - qlen[r]:seq[r]] for r in reqs]).to(dev)
+                vn = torch.cat([V[layer][r][seq[r] - qlen[r]:seq[r]] for r in reqs]).to(dev)
+                with override_forward_context(types.SimpleNamespace(attn_metadata={name: meta})):
+                    impl.do_kv_cache_update(lay, kn, vn, caches[layer], slots)
                 out = torch.zeros(int(qsl[-1]) + 4, h, d, dtype=torch.bfloat16, device=dev)
-                impl.forward(types.SimpleNamespace(layer_name=f"model.layers.{layer}.self_attn.attn"),
-                             q.to(dev), kn.to(dev), vn.to(dev), caches[layer], meta, out)
+                impl.forward(lay, q.to(dev), kn, vn, caches[layer], meta, out)
                 torch.cuda.synchronize()
                 got = out.float().cpu().numpy()
                 for i, r in enumerate(reqs):
@@ -221,8 +230,13 @@ def test_backend_decode_ring_mixed_batch_one_gpu():
                     worst = max(worst, err)
         assert rb.IMPL_STATS["decode_ring"] == steps * layers
         assert ring.lens[0][1] == own0 + steps          # own chunk + every decode token (one rank)
+        assert rb.WRITE_TRACK["skipped"] == steps * layers
+        p0 = torch.arange(own0, own0 + steps)
+        for layer in range(layers):                      # the ring's tokens are not in this pool
+            assert torch.all(caches[layer][bt[0, p0 // bs].long().to(dev), :, (p0 % bs).to(dev)] == 0)
     finally:
         rb.DECODE_RING_MAP.clear()
+        rb.WRITE_TRACK["enabled"] = False
 
 
 @pytest.mark.gpu
@@ -253,3 +267,45 @@ def test_backend_decode_ring_nccl_two_gpus():
             outs.append(p.communicate()[0])
     assert all(p.returncode == 0 for p in procs), "\n".join(o[-3000:] for o in outs)
     assert '"ok": true' in outs[1], outs[1][-3000:]
+
+
+def test_pool_write_skips_decode_ring_tokens(monkeypatch):
+    """``do_kv_cache_update`` does not write a decode-ring request's new
+    token into this pool (its assignee keeps it, ``ring_backend.py:519-531``);
+    every other row is written, and ``WRITE_TRACK`` records both."""
+    from vllm.forward_context import override_forward_context
+
+    from hcp_vllm_plugin_b200 import ops
+    from hcp_vllm_plugin_b200 import ring_backend as rb
+
+    def cpu_scatter(key, value, cache, slots):
+        for i, s in enumerate(slots.tolist()):
+            if s >= 0:
+                cache[s // BS, :, s % BS, :D] = key[i]
+                cache[s // BS, :, s % BS, D:] = value[i]
+
+    monkeypatch.setattr(ops, "kv_cache_update", cpu_scatter)
+    rb.DECODE_RING_MAP.clear()
+    rb.register_decode_ring(7, ring=None, slot=0, prefix_len=0)
+    name = "model.layers.0.self_attn.attn"
+    # rows: ring decode (block 7), plain decode (block 3), a 3-token prefill (block 9)
+    meta = types.SimpleNamespace(query_start_loc=torch.tensor([0, 1, 2, 5]), seq_lens=torch.tensor([10, 6, 3]),
+                                 block_table=torch.tensor([[7, 8, 0], [2, 3, 0], [9, 0, 0]], dtype=torch.int32))
+    slots = torch.tensor([7 * BS + 1, 3 * BS + 1, 9 * BS, 9 * BS + 1, 9 * BS + 2])
+    cache = torch.zeros(10, HKV, BS, 2 * D)
+    key, value = torch.ones(5, HKV, D), torch.full((5, HKV, D), 2.0)
+    impl = rb.HcpRingAttentionImpl(H, D, D ** -0.5, HKV)
+    rb.reset_write_tracking()
+    try:
+        with override_forward_context(types.SimpleNamespace(attn_metadata={name: meta})):
+            impl.do_kv_cache_update(types.SimpleNamespace(layer_name=name), key, value, cache, slots)
+        assert torch.all(cache[7] == 0)                       # the ring token went nowhere here
+        for s in slots.tolist()[1:]:
+            assert torch.all(cache[s // BS, :, s % BS, :D] == 1) and torch.all(cache[s // BS, :, s % BS, D:] == 2)
+        assert rb.WRITE_TRACK["skipped"] == 1 and rb.WRITE_TRACK["slots"] == set(slots.tolist()[1:])
+        # without a forward context nothing can be attributed: every row is written
+        impl.do_kv_cache_update(types.SimpleNamespace(layer_name=name), key, value, cache, slots)
+        assert torch.all(cache[7, :, 1, :D] == 1)
+    finally:
+        rb.DECODE_RING_MAP.clear()
+        rb.WRITE_TRACK["enabled"] = False
