@@ -126,15 +126,37 @@ def reset_impl_stats() -> None:
 # ``installed`` (layers whose own chunk is in the slot already).
 # ---------------------------------------------------------------------------
 DECODE_RING_MAP: dict[int, dict] = {}
+# The connector's refcount-aware release of a request's staged prefix, called
+# at the request's first decode step (ring_backend.py:156-157, 213-225).
+_STAGING_RELEASE_FN = None
 
 
 def _decode_ring_enabled() -> bool:
     return os.environ.get("HCP_RING_DECODE_RING", "1") == "1"
 
 
+def set_staging_release_fn(fn) -> None:
+    global _STAGING_RELEASE_FN
+    _STAGING_RELEASE_FN = fn
+
+
+def _release_staged_for_request(first_block_id: int) -> None:
+    """Decode-ring transition: the staged prefix of this request is not read
+    again (the peers hold it), so it is freed now, through the connector when
+    it registered a release function."""
+    if first_block_id not in PEER_REQ_MAP:
+        return
+    if _STAGING_RELEASE_FN is not None:
+        _STAGING_RELEASE_FN(first_block_id)
+    else:
+        for ck in PEER_REQ_MAP.pop(first_block_id, None) or []:
+            drop_chunk_kv(ck)
+
+
 def register_decode_ring(first_block_id: int, ring, slot: int, prefix_len: int) -> None:
     DECODE_RING_MAP[first_block_id] = {"ring": ring, "slot": int(slot), "prefix_len": int(prefix_len),
-                                       "own_len": None, "installed": set()}
+                                       "first_block_id": int(first_block_id), "own_len": None,
+                                       "installed": set()}
 
 
 def clear_decode_ring(first_block_id: int) -> None:
@@ -414,6 +436,9 @@ class HcpRingAttentionImpl(AttentionImpl):
                 positions.append(tk - 1)
             if li == 0:
                 ring.begin_step(slots, positions, fresh)
+                for _, e in rows:
+                    if not e["installed"]:
+                        _release_staged_for_request(e["first_block_id"])
             for r, e in rows:
                 if li not in e["installed"]:
                     self._install_own_chunk(ring, li, r, e, kv_cache, block_table)

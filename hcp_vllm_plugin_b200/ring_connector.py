@@ -68,6 +68,7 @@ from .ring_backend import (
     drop_chunk_kv,
     map_request_peer,
     register_decode_ring,
+    set_staging_release_fn,
     stage_peer_kv,
     unmap_request_peer,
 )
@@ -285,6 +286,9 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         self._decode_slots = int(cfg.get_from_extra_config("ring_decode_slots", 4))
         self._decode_capacity = int(cfg.get_from_extra_config("ring_decode_capacity", 17408))
         self._decode_backend = str(cfg.get_from_extra_config("ring_decode_backend", "nccl"))
+        # the chunk a peer serves (the reference's ring_partial_chunks, first entry)
+        self._decode_chunk_key = (as_str_list(cfg.get_from_extra_config("ring_partial_chunks", ""))
+                                  or [self._chunk_id])[0]
         self._decode_on = bool(self._decode_addr) and decode_ring_on() and \
             0 <= self._decode_rank < self._decode_world
         self._decode_owner = self._decode_on and self._decode_rank == self._decode_world - 1
@@ -295,7 +299,7 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         self._drop_consumed = self._decode_on
         self._decode_ring = None
         self._decode_free_slots = list(range(self._decode_slots))
-        self._decode_slot_of: dict[str, int] = {}
+        self._decode_slot_of: dict[str, tuple[int, int]] = {}   # req -> (slot, first block id)
         self._decode_stop = threading.Event()
         self._decode_thread: threading.Thread | None = None
         self._decode_error: BaseException | None = None
@@ -313,6 +317,9 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         self._store_slots: dict[str, tuple] = {}         # producer: chunk -> (host, device) slots
         self._saved_layers: dict[str, set[int]] = {}
         os.makedirs(self._run_dir(), exist_ok=True)
+        if self._role == KVConnectorRole.WORKER:
+            # the backend frees a request's staging at its first decode step
+            set_staging_release_fn(self._release_request_staging)
         if self._decode_on and not self._decode_owner and self._role == KVConnectorRole.WORKER:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() \
                 else torch.device("cpu")
@@ -339,9 +346,9 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         """This node's chunk for ``layer``, out of its chunk store (the
         reference's node serves its own chunk snapshot,
         ``ring_decode.py:246-249``)."""
-        store = self._stores.get(self._chunk_id)
+        store = self._stores.get(self._decode_chunk_key)
         if store is None:
-            raise RuntimeError(f"HcpRingKvConnector: decode ring peer has no saved chunk {self._chunk_id}")
+            raise RuntimeError(f"HcpRingKvConnector: decode ring peer has no saved chunk {self._decode_chunk_key}")
         return store[layer, 0], store[layer, 1]
 
     def _serve_decode_ring(self, device: torch.device) -> None:
@@ -368,7 +375,7 @@ class HcpRingKvConnector(KVConnectorBase_V1):
             raise RuntimeError(f"HcpRingKvConnector: all {self._decode_slots} decode ring slots are in use "
                                "(ring_decode_slots)")
         slot = self._decode_free_slots.pop(0)
-        self._decode_slot_of[req.req_id] = slot
+        self._decode_slot_of[req.req_id] = (slot, req.first_block_id)
         register_decode_ring(req.first_block_id, self._decode_ring, slot, expected)
 
     # ------------------------------------------------------------------ paths
@@ -625,21 +632,29 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         self._cleanup_finished(finished_req_ids)
         return None, None
 
-    def _release_live_entry(self, req_id: str) -> None:
+    def _release_request_staging(self, first_block_id: int) -> None:
+        """Backend callback at a decode-ring request's first decode step:
+        free its staged prefix (refcounted) and keep its ring registration
+        for the decode phase (``ring_connector.py:978-987``)."""
+        req_id = next((rid for rid, (fb, _) in self._live.items() if fb == first_block_id), None)
+        if req_id is not None:
+            self._release_live_entry(req_id, clear_ring=False)
+
+    def _release_live_entry(self, req_id: str, clear_ring: bool = True) -> None:
         st = self._streams.pop(req_id, None)
         if st is not None:
             st.done.set()
             if st.thread is not None:
                 st.thread.join()
+        if clear_ring and req_id in self._decode_slot_of:
+            slot, fb = self._decode_slot_of.pop(req_id)
+            clear_decode_ring(fb)
+            self._decode_free_slots.append(slot)
         live = self._live.pop(req_id, None)
         if live is None:
             return
         first_block_id, chunk_keys = live
         unmap_request_peer(first_block_id)
-        slot = self._decode_slot_of.pop(req_id, None)
-        if slot is not None:
-            clear_decode_ring(first_block_id)
-            self._decode_free_slots.append(slot)
         for ck in chunk_keys:
             refs = self._chunk_refs.get(ck, 0) - 1
             if refs <= 0:
@@ -657,8 +672,11 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         return None
 
     def shutdown(self) -> None:
-        for req_id in list(self._live):
+        for req_id in list(self._live) + list(self._decode_slot_of):
             self._release_live_entry(req_id)
+        from . import ring_backend
+        if ring_backend._STAGING_RELEASE_FN == self._release_request_staging:
+            set_staging_release_fn(None)
         if self._decode_owner and self._decode_ring is not None:
             self._decode_ring.stop()          # ends the peers' serve loops
         self._decode_stop.set()

@@ -91,8 +91,11 @@ def _body(rank, port):
                 c[b, :, o, :D] = own[r][layer][0][j]
                 c[b, :, o, D:] = own[r][layer][1][j]
         caches.append(c)
+    released = []
+    rb.set_staging_release_fn(released.append)
     for r in range(2):
         rb.register_decode_ring(int(bt[r, 0]), ring, slot=r, prefix_len=PREFIX)
+        rb.map_request_peer(int(bt[r, 0]), ["c0"])      # its prefix was staged for the prefill
     worst = 0.0
     for t in range(STEPS):
         seq = [PREFIX + n + t + 1 for n in OWN]
@@ -115,7 +118,8 @@ def _body(rank, port):
     comm.close()
     for r in range(2):
         rb.clear_decode_ring(int(bt[r, 0]))
-    return {"worst": worst, "ring_steps": rb.IMPL_STATS["decode_ring"],
+    return {"worst": worst, "ring_steps": rb.IMPL_STATS["decode_ring"], "released": released,
+            "first_blocks": [int(bt[r, 0]) for r in range(2)],
             "growth": [ring.growth_positions[0][r] for r in range(2)]}
 
 
@@ -137,6 +141,8 @@ def test_backend_routes_decode_rows_to_the_ring():
     owner = res[1]
     assert owner["worst"] < 1e-5, owner
     assert owner["ring_steps"] == STEPS * LAYERS
+    # each request's staged prefix is released once, at its first decode step
+    assert owner["released"] == owner["first_blocks"]
     # the owner (rank 1 of 2) keeps the decode tokens at odd positions
     for r, n in enumerate(OWN):
         pos = [PREFIX + n + t for t in range(STEPS)]

@@ -210,7 +210,12 @@ def test_streaming_window_and_refcounts(tmp_path, monkeypatch, window):
         assert min(layers_staged) >= i
         assert max(layers_staged) <= i + window + 1
     assert rb.STAGING_STATS["max_staged_layers"] <= (window + 2) * 2
-    # r0 finishes: c1 (only r0) is dropped, c0 (shared with r1) stays
+    # r0 starts decoding: the backend frees its staging (c1 is r0's only, c0
+    # is shared with r1) and its ring registration stays (ring_connector.py:978-987)
+    rb._release_staged_for_request(3)
+    assert 3 not in rb.PEER_REQ_MAP and 9 in rb.PEER_REQ_MAP and 3 in rb.DECODE_RING_MAP
+    assert not any(key[0] == "c1" for key in rb.PEER_KV_STAGING) and conn._chunk_refs == {"c0": 1}
+    # r0 finishes: its ring slot is released, c0 (shared with r1) stays
     conn.bind_connector_metadata(_load_meta([], finished=["r0"]))
     conn.start_load_kv(fk.forward_context({}))
     assert 3 not in rb.PEER_REQ_MAP and 9 in rb.PEER_REQ_MAP
