@@ -146,3 +146,83 @@ def test_decode_ring_owner_alone(world):
     want, _ = ro.attn_with_lse(qq.numpy(), torch.cat([own["A"][0][0], kn]).numpy(),
                                torch.cat([own["A"][0][1], vn]).numpy(), D ** -0.5, None)
     assert np.abs(out.numpy() - want).max() < 1e-5
+
+
+# ---------------------------------------------------------------------------
+# failure paths on the host: a dead peer, a silent owner
+# ---------------------------------------------------------------------------
+def _dead_peer_rank(rank, port, q):
+    """Rank 0 joins the ring and exits without serving; rank 1 (the owner)
+    must get an error from its step within the group's timeout."""
+    import time
+
+    from hcp_vllm_plugin_b200.ring_decode import RingComm
+    RingDecode = _cpu_ops()
+    comm = RingComm.standalone("127.0.0.1", port, rank, 2, backend="gloo", timeout_s=5, connect_timeout_s=60)
+    ring = RingDecode(1, 1, 8, H, HKV, D, D ** -0.5, torch.device("cpu"), dtype=torch.float32, comm=comm)
+    if rank == 0:
+        q.put((rank, "left"))
+        return
+    time.sleep(1.0)
+    t0 = time.time()
+    ring.begin_step([0], [5], [0])
+    try:
+        ring.step(0, [5], torch.randn(1, H, D), torch.randn(1, HKV, D), torch.randn(1, HKV, D),
+                  torch.empty(1, H, D), slots=[0])
+        q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001 - the expected failure
+        q.put((rank, ("error", time.time() - t0, type(e).__name__)))
+
+
+def test_owner_step_fails_when_a_peer_is_gone():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_dead_peer_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[0] == "left"
+    assert isinstance(res[1], tuple) and res[1][0] == "error", res[1]
+    assert res[1][1] < 60, res[1]                 # bounded by the group's timeout, no hang
+
+
+def _silent_owner_rank(rank, port, q):
+    """The owner joins and never posts a step; the peer's serve loop keeps
+    polling the store and returns once its stop event is set."""
+    import threading
+    import time
+
+    from hcp_vllm_plugin_b200.ring_decode import RingComm
+    RingDecode = _cpu_ops()
+    comm = RingComm.standalone("127.0.0.1", port, rank, 2, backend="gloo", timeout_s=30, connect_timeout_s=60)
+    ring = RingDecode(1, 1, 8, H, HKV, D, D ** -0.5, torch.device("cpu"), dtype=torch.float32, comm=comm)
+    if rank == 1:
+        time.sleep(3.0)                            # stay in the group while the peer polls
+        q.put((rank, "done"))
+        return
+    stop = threading.Event()
+    threading.Timer(1.0, stop.set).start()
+    t0 = time.time()
+    ring.serve(lambda layer: (torch.zeros(1, HKV, D), torch.zeros(1, HKV, D)), stop=stop, poll_s=0.2)
+    q.put((rank, (ring.steps_served, time.time() - t0)))
+
+
+def test_peer_serve_loop_stops_without_an_owner_step():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_silent_owner_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    steps, waited = res[0]
+    assert steps == 0 and 0.9 < waited < 10, res[0]
