@@ -533,12 +533,12 @@ class HcpRingKvConnector(KVConnectorBase_V1):
             self._side_stream = torch.cuda.Stream(device=device)
         for req in need:
             expected = align_down(req.prefix_len or self._prefix_len, self._block_size)
+            if self._decode_owner:
+                self._register_decode(req, expected, device)   # may fail: before any other state
             map_request_peer(req.first_block_id, req.chunk_keys)
             self._live[req.req_id] = (req.first_block_id, list(req.chunk_keys))
             for ck in req.chunk_keys:
                 self._chunk_refs[ck] = self._chunk_refs.get(ck, 0) + 1
-            if self._decode_owner:
-                self._register_decode(req, expected, device)
             st = _PrefillStream(req.req_id, layer_order, list(req.chunk_keys), expected)
             self._streams[req.req_id] = st
             st.thread = threading.Thread(target=self._stream_worker, args=(st, device), daemon=True)

@@ -507,3 +507,19 @@ def test_connector_staging_feeds_backend_forward(tmp_path):
     cons.shutdown()
     for prod in producers:
         prod.shutdown()
+
+
+def test_decode_ring_slots_exhausted(tmp_path):
+    """More decode-ring requests than ``ring_decode_slots`` at once is an
+    error, not a shared slot."""
+    from hcp_vllm_plugin_b200 import ring_backend as rb
+
+    STORES.clear()
+    STORES["c0"] = torch.zeros(2, 2, 16, 2, 8)
+    _write_marker(str(tmp_path), "c0", STORES["c0"])
+    conn = _consumer(str(tmp_path), 2, dict(OWNER, ring_decode_slots=1))
+    conn.bind_connector_metadata(_load_meta([("r0", 1, ["c0"], 16), ("r1", 2, ["c0"], 16)]))
+    with pytest.raises(RuntimeError, match="slots"):
+        conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in _layers(2)}))
+    assert list(conn._live) == ["r0"] and 2 not in rb.PEER_REQ_MAP   # r1 left no state behind
+    conn.shutdown()
