@@ -63,6 +63,12 @@ constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
 constexpr float kRescaleThreshold = 8.0f;            // log2 units
 constexpr int kPreciseKeys = 256;  // rows seeing fewer keys get the hi+lo P product
+// Named barriers of the NB issuer protocol: event barrier of query tile x
+// (softmax warpgroup x arrives, the MMA warp syncs) and its acknowledgement
+// (the MMA warp arrives, the warpgroup syncs); 128 + 32 threads each.
+constexpr int kNbEvent0 = 1;
+constexpr int kNbAck0 = 3;
+constexpr int kNbThreads = 160;
 
 // Failure codes written to g_device_status.
 enum : int {
@@ -210,7 +216,11 @@ struct FwdSmem {
   static constexpr int kBytes = kEnd + 1024;  // + alignment slack
 };
 
-template <int D, bool F16>
+// NB selects how the MMA issuer synchronises with the softmax warpgroups:
+// false - it waits on mbarriers (P ready, K / V tiles landed);
+// true  - it meets the softmax warpgroups only at named barriers, and they
+//         do the mbarrier waits for the tiles their P feeds (see below).
+template <int D, bool F16, bool NB = false>
 __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_constant__ FwdParams p) {
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
   using L = FwdSmem<D>;
@@ -391,6 +401,77 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     }
   } else if (warp == kWarpMma) {
     // ================================================================ MMA issuer
+    if constexpr (NB) {
+    // Events of query tile x, in order: K(a0) before its first QK; after it
+    // each P(t) (P_x of tile t stored, V(t) landed, and K(t+1) landed when
+    // tile t+1 is x's next) before PV_x(t); and a K(t') event before QK_x(t')
+    // when x's next tile t' is not t+1.  Each event: bar.sync on the event
+    // barrier, bar.arrive on its ack, so warpgroup and issuer stay in
+    // lockstep.  No mbarrier wait here: those would stall the pipe.
+    int pv_count[2] = {0, 0};
+    for (int t = 0; t <= n_tiles; ++t) {
+      const bool have_prev = t >= 1;
+      const bool have_cur = t < n_tiles;
+      const int sp = (t - 1) % kStages;
+      const int sc = t % kStages;
+      for (int x = 0; x < 2; ++x) {
+        const bool pv = have_prev && active(x, t - 1);
+        if (pv) {
+          ptx::named_bar_sync(kNbEvent0 + x, kNbThreads);
+          ptx::named_bar_arrive(kNbAck0 + x, kNbThreads);
+          ptx::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t s_v = s_kv0 + (2 * sp + 1) * kTileBytes;
+            const uint32_t o_acc = tmem + 256 + x * D;
+            const uint32_t p_col = tmem + x * 128;
+#pragma unroll
+            for (int kk = 0; kk < kBlockN / 16; ++kk) {
+              const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
+              ptx::umma_ts(o_acc, p_col + kk * 8, bdesc, kIdescPV, (pv_count[x] > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (x == 0 ? precise_a : precise_b) {
+#pragma unroll
+              for (int kk = 0; kk < kBlockN / 16; ++kk) {
+                const uint64_t bdesc = ptx::sdesc_sw128(s_v + kk * 2048, kBoxBytes, 1024);
+                ptx::umma_ts(o_acc, p_col + 64 + kk * 8, bdesc, kIdescPV, 1u);
+              }
+            }
+            ptx::umma_commit(b_odone(x));
+          }
+          __syncwarp();
+          ++pv_count[x];
+        }
+        if (have_cur && active(x, t)) {
+          if (!pv) {  // K(t) event: x's first tile, or its next tile after a gap
+            ptx::named_bar_sync(kNbEvent0 + x, kNbThreads);
+            ptx::named_bar_arrive(kNbAck0 + x, kNbThreads);
+            ptx::tc_fence_after();
+          }
+          if (lane == 0) {
+            const uint32_t s_k = s_kv0 + (2 * sc) * kTileBytes;
+            const uint32_t s_qx = s_q + x * kTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
+              const uint64_t adesc = ptx::sdesc_sw128(s_qx + off, 16, 1024);
+              const uint64_t bdesc = ptx::sdesc_sw128(s_k + off, 16, 1024);
+              ptx::umma_ss(tmem + x * 128, adesc, bdesc, kIdescQK, kk > 0 ? 1u : 0u);
+            }
+            ptx::umma_commit(b_sfull(x));
+          }
+          __syncwarp();
+        }
+      }
+      if (lane == 0) {
+        if (have_prev) ptx::umma_commit(b_vempty(sp));
+        if (have_cur) ptx::umma_commit(b_kempty(sc));
+      }
+      __syncwarp();
+    }
+    if (lane == 0) ptx::umma_commit(b_final);
+    __syncwarp();
+    drain_bar(b_final, 0);
+    } else {
     bool ok = __all_sync(0xffffffffu, wait_bar(b_q, 0, abort_flag, kErrWaitMma));
     int pv_count[2] = {0, 0};  // PV products issued per query tile
     for (int t = 0; t <= n_tiles && ok; ++t) {
@@ -468,6 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     if (lane == 0) ptx::umma_commit(b_final);
     __syncwarp();
     drain_bar(b_final, 0);
+    }
   } else {
     // ================================================================ softmax + epilogue
     const int x = warp >> 2;                 // query tile of this warpgroup (0 = A, 1 = B)
@@ -483,6 +565,139 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     float l = 0.f;             // row sum
     bool ok = true;
     int done = 0;              // KV tiles processed by this warpgroup
+    if constexpr (NB) {
+    // Events for the issuer, in its order (see the MMA issuer): K(a0), then
+    // per tile P(t) - with K(t+1) folded in when t+1 is this tile's next -
+    // and a separate K event before a next tile after a gap.  Every event is
+    // executed even after a failed wait (the work is skipped, never a
+    // barrier), so the named barriers always pair up.
+    auto next_active = [&](int t) {
+      int u = t + 1;
+      while (u < n_tiles && !active(x, u)) ++u;
+      return u;
+    };
+    auto kv_phase = [&](int t) { return static_cast<uint32_t>((t / kStages) & 1); };
+    const int first = next_active(-1);
+    if (first < n_tiles) {
+      ok = __all_sync(0xffffffffu, wait_bar(b_q, 0, abort_flag, kErrWaitSoftmax));
+      if (ok)
+        ok = __all_sync(0xffffffffu,
+                        wait_bar(b_kfull(first % kStages), kv_phase(first), abort_flag, kErrWaitSoftmax));
+      ptx::tc_fence_before();
+      ptx::named_bar_arrive(kNbEvent0 + x, kNbThreads);            // K(a0)
+    }
+    for (int t = first; t < n_tiles; t = next_active(t)) {
+      if (ok) ok = __all_sync(0xffffffffu, wait_bar(b_sfull(x), done & 1, abort_flag, kErrWaitSoftmax));
+      if (ok) {
+        ptx::tc_fence_after();
+        const int key0 = tile_key0(t);
+        const hcp_kv_segment& seg = wk.seg[tile_seg(t)];
+        int vis = seg.len - key0;
+        if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
+        vis = max(0, min(vis, kBlockN));
+
+        uint32_t sr[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          ptx::tmem_ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+        ptx::tmem_wait_ld();
+        if (vis < kBlockN) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= vis) sr[i] = __float_as_uint(-INFINITY);
+        }
+        float mx8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = __uint_as_float(sr[j]);
+#pragma unroll
+        for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float mx2 = mx * scale_log2;  // -inf stays -inf
+        const bool raise = mx2 > m_used + kRescaleThreshold;
+        const float m_new = raise ? mx2 : m_used;
+        const float alpha = raise ? ex2_approx(m_used - m_new) : 1.f;  // 0 when m_used = -inf
+        const float m_base = (m_new == -INFINITY) ? 0.f : m_new;
+        float sums[4] = {0.f, 0.f, 0.f, 0.f};
+        if (!precise) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
+              const float p1 =
+                  ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+              sums[i & 3] += p0 + p1;
+              pk[i] = pack2<F16>(p0, p1);
+            }
+            ptx::tmem_st_32x32b_x16(s_addr + c * 16, pk);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t pk[16], pl[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
+              const float p1 =
+                  ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+              sums[i & 3] += p0 + p1;
+              pk[i] = pack2<F16>(p0, p1);
+              const float2 h2 = unpack2<F16>(pk[i]);
+              pl[i] = pack2<F16>(p0 - h2.x, p1 - h2.y);
+            }
+            ptx::tmem_st_32x32b_x16(s_addr + c * 16, pk);
+            ptx::tmem_st_32x32b_x16(s_addr + 64 + c * 16, pl);
+          }
+        }
+        l = l * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
+        m_used = m_new;
+        if (done >= 1) {
+          ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), (done - 1) & 1, abort_flag, kErrWaitSoftmax));
+          if (ok) {
+            ptx::tc_fence_after();
+            if (__any_sync(0xffffffffu, raise)) {
+#pragma unroll
+              for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                ptx::tmem_ld_32x32b_x32(o_addr + c * 32, o);
+                ptx::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                ptx::tmem_st_32x32b_x32(o_addr + c * 32, o);
+              }
+            }
+          }
+        }
+      }
+      const int nt = next_active(t);
+      const bool merged = nt == t + 1 && nt < n_tiles;
+      // the tiles the issuer reads after this event: V(t), and K(t+1) if merged
+      if (ok) ok = __all_sync(0xffffffffu, wait_bar(b_vfull(t % kStages), kv_phase(t), abort_flag, kErrWaitSoftmax));
+      if (ok && merged)
+        ok = __all_sync(0xffffffffu, wait_bar(b_kfull(nt % kStages), kv_phase(nt), abort_flag, kErrWaitSoftmax));
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::named_bar_sync(kNbAck0 + x, kNbThreads);
+      ptx::named_bar_arrive(kNbEvent0 + x, kNbThreads);            // P(t)
+      ++done;
+      if (nt < n_tiles && !merged) {
+        if (ok)
+          ok = __all_sync(0xffffffffu, wait_bar(b_kfull(nt % kStages), kv_phase(nt), abort_flag, kErrWaitSoftmax));
+        ptx::tc_fence_before();
+        ptx::named_bar_sync(kNbAck0 + x, kNbThreads);
+        ptx::named_bar_arrive(kNbEvent0 + x, kNbThreads);          // K(nt)
+      }
+    }
+    if (first < n_tiles) {
+      if (ok && done > 0) {
+        ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), (done - 1) & 1, abort_flag, kErrWaitSoftmax));
+        ptx::tc_fence_after();
+      }
+      ptx::named_bar_sync(kNbAck0 + x, kNbThreads);                // ack of the last event
+    }
+    } else {
     for (int t = 0; t < n_tiles; ++t) {
       if (!active(x, t)) continue;
       ok = __all_sync(0xffffffffu, wait_bar(b_sfull(x), done & 1, abort_flag, kErrWaitSoftmax));
@@ -578,6 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     if (ok && done > 0) {
       ok = __all_sync(0xffffffffu, wait_bar(b_odone(x), (done - 1) & 1, abort_flag, kErrWaitSoftmax));
       ptx::tc_fence_after();
+    }
     }
     if (ok) {
       // ---------------------------------------------------------- epilogue

@@ -50,6 +50,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// ------------------------------------------------------- named barriers
+// CTA-wide hardware barriers 1..15 (0 is __syncthreads).  `count` threads
+// take part, a multiple of 32; whole warps execute these (aligned forms).
+// Unlike mbarrier waits, a bar.sync does not stall a warp's earlier
+// tcgen05.mma instructions from being taken by the tensor pipe.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
