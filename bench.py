@@ -192,6 +192,7 @@ def main():
     ap.add_argument("--kernel", choices=["fwd", "decode"], default=None,
                     help="profiling mode: time one kernel on a small case and exit")
     ap.add_argument("--decode-seqs", type=int, default=16)
+    ap.add_argument("--iters", type=int, default=1, help="timed launches in --kernel mode")
     ap.add_argument("--rows", action="store_true",
                     help="measure the connector / decode-ring rows instead of the headline")
     args = ap.parse_args()
@@ -410,7 +411,32 @@ def side_configs(dev, pk):
     byts = B * (LOC + PEER) * HKV * D * 2 * 2
     res["cfg2_splitkv_decode"] = {"ms": ms2, "gbs": byts / ms2 / 1e6, "algorithmic_bytes": byts,
                                   "frac_of_hbm": byts / ms2 / 1e6 / pk["hbm_gbs"]}
+    res["fwd_issuer_variants_16k_causal"] = fwd_issuer_variants(16384)
     return res
+
+
+def fwd_issuer_variants(seq: int) -> dict:
+    """The forward kernel on one ``seq``-token causal launch with the default
+    (mbarrier) MMA issuer and with the named-barrier issuer
+    (``HCP_FWD_NAMED_BARRIERS=1``), each in a fresh process, since the library
+    reads the switch once per process.  Reported beside the headline only."""
+    out = {}
+    for name, flag in (("mbarrier_issuer", "0"), ("named_barrier_issuer", "1")):
+        env = dict(os.environ, HCP_FWD_NAMED_BARRIERS=flag)
+        cmd = [sys.executable, os.path.abspath(__file__), "--kernel", "fwd", "--seq", str(seq), "--iters", "5"]
+        try:
+            r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=180)
+        except subprocess.TimeoutExpired:
+            out[name] = {"error": "timeout"}
+            continue
+        line = [x for x in r.stdout.splitlines() if x.startswith("kernel=")]
+        if r.returncode != 0 or not line:
+            out[name] = {"error": (r.stdout + r.stderr)[-300:]}
+            continue
+        kv = dict(f.split("=", 1) for f in line[-1].split()[1:])
+        out[name] = {"ms": float(kv["ms"]), "tflops": float(kv["TFLOP/s"]),
+                     "device_status": int(kv["device_status"])}
+    return out
 
 
 def run_kernel(args):
@@ -456,10 +482,11 @@ def run_kernel(args):
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    fn()
+    for _ in range(max(1, args.iters)):
+        fn()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b)
+    ms = a.elapsed_time(b) / max(1, args.iters)
     rate = work_units / ms / (1e9 if unit == "TFLOP/s" else 1e6)
     print(f"kernel={args.kernel} ms={ms:.3f} {unit}={rate:.1f} device_status={C.device_status()}", flush=True)
 
