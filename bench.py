@@ -318,6 +318,10 @@ def main():
         e2e = run_e2e(args, runner, dev, chunk, L, barrier, max_over_ranks, world)
 
     side = side_configs(dev, pk) if (world == 1 and not args.no_side) else None
+    if not args.no_side:
+        # the decode ring's step on the same ranks (collective: every rank)
+        ring_dec = decode_ring_step(world, rank, dev, pk, torch.Generator(device=dev).manual_seed(5), barrier)
+        side = dict(side or {}, decode_ring_step=ring_dec)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -491,6 +495,52 @@ def run_kernel(args):
     print(f"kernel={args.kernel} ms={ms:.3f} {unit}={rate:.1f} device_status={C.device_status()}", flush=True)
 
 
+def decode_ring_step(world, rank, dev, pk, g, barrier) -> dict:
+    """One ``RingDecode.step`` over all ranks (collective: every rank calls
+    it): 64 requests x 65536 context keys split over the ranks, one layer,
+    CUDA events, max over ranks.  Warm-up covers max(3, N) steps so every
+    rank has kept a decode token (the growth append's kernels are loaded)
+    before timing."""
+    import torch
+    import torch.distributed as dist
+
+    from hcp_vllm_plugin_b200.ring_decode import RingDecode
+
+    B, total, warm, steps = 64, 65536, max(3, world), 10
+    chunk = total // world
+    rd = RingDecode(1, B, chunk + warm + steps + 1, H, HKV, D, D ** -0.5, dev)
+    for b in range(B):
+        base = b * rd.cap
+        rd.k[0, base:base + chunk].normal_(generator=g)
+        rd.v[0, base:base + chunk].normal_(generator=g)
+        rd.lens[0][b] = chunk
+    q = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    kn = torch.empty(B, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    vn = torch.empty_like(kn).normal_(generator=g)
+    out = torch.empty(B, H, D, device=dev)
+    owner = rank == rd.owner
+    args = (q, kn, vn, out) if owner else (None, None, None, None)
+    for s in range(warm):
+        rd.step(0, [total + s] * B, *args)
+    barrier()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for s in range(warm, warm + steps):
+        rd.step(0, [total + s] * B, *args)
+    b_.record()
+    barrier()
+    ms = a.elapsed_time(b_) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    kv_bytes = B * (total + warm + steps // 2) * HKV * D * 2 * 2
+    del rd
+    return {"ms_per_step": ms, "requests": B, "context_keys": total, "ranks": world,
+            "kv_gbs_all_ranks": kv_bytes / ms / 1e6,
+            "frac_of_hbm_all_ranks": kv_bytes / ms / 1e6 / (pk["hbm_gbs"] * world)}
+
+
 def run_rows(args, world, rank, local_rank):
     """``--rows``: one JSON line with device-timed measurements of the rows
     beside the forward kernel (CUDA events, max over ranks where collective):
@@ -519,7 +569,6 @@ def run_rows(args, world, rank, local_rank):
 
     from hcp_vllm_plugin_b200 import _capi as C
     from hcp_vllm_plugin_b200 import ops
-    from hcp_vllm_plugin_b200.ring_decode import RingDecode
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -577,41 +626,7 @@ def run_rows(args, world, rank, local_rank):
             res["f3_merge_n"] = {"error": repr(e)}
 
     # f3: ring decode over all ranks
-    # every rank receives a decode token within the first N warm-up steps
-    B, total, warm, steps = 64, 65536, max(3, world), 10
-    chunk = total // world
-    rd = RingDecode(1, B, chunk + warm + steps + 1, H, HKV, D, D ** -0.5, dev)
-    for b in range(B):
-        base = b * rd.cap
-        rd.k[0, base:base + chunk].normal_(generator=g)
-        rd.v[0, base:base + chunk].normal_(generator=g)
-        rd.lens[0][b] = chunk
-    q = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
-    kn = torch.empty(B, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
-    vn = torch.empty_like(kn).normal_(generator=g)
-    out = torch.empty(B, H, D, device=dev)
-    owner = rank == rd.owner
-    for s in range(warm):
-        rd.step(0, [total + s] * B, q if owner else None, kn if owner else None, vn if owner else None,
-                out if owner else None)
-    barrier()
-    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for s in range(warm, warm + steps):
-        rd.step(0, [total + s] * B, q if owner else None, kn if owner else None, vn if owner else None,
-                out if owner else None)
-    b_.record()
-    barrier()
-    ms = a.elapsed_time(b_) / steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    kv_bytes = B * (total + warm + steps // 2) * HKV * D * 2 * 2
-    res["f3_ring_decode"] = {"ms_per_step": ms, "requests": B, "context_keys": total, "ranks": world,
-                             "kv_gbs_all_ranks": kv_bytes / ms / 1e6,
-                             "frac_of_hbm_all_ranks": kv_bytes / ms / 1e6 / (pk["hbm_gbs"] * world)}
-    del rd
+    res["f3_ring_decode"] = decode_ring_step(world, rank, dev, pk, g, barrier)
 
     if world > 1:  # f1: CUDA IPC copy from rank 0's store to rank 1
         nbytes = 2 << 30
