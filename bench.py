@@ -428,13 +428,16 @@ def side_configs(dev, pk):
 
 
 def fwd_issuer_variants(seq: int) -> dict:
-    """The forward kernel on one ``seq``-token causal launch with the default
-    (mbarrier) MMA issuer and with the named-barrier issuer
-    (``HCP_FWD_NAMED_BARRIERS=1``), each in a fresh process, since the library
-    reads the switch once per process.  Reported beside the headline only."""
+    """The forward kernel on one ``seq``-token causal launch in each variant:
+    the default (mbarrier) MMA issuer, the named-barrier issuer
+    (``HCP_FWD_NAMED_BARRIERS=1``) and the named-barrier issuer with a quarter
+    of the exponentials on the FMA pipe (``HCP_FWD_POLY_EXP2=1``), each in a
+    fresh process, since the library reads the switches once per process.
+    Reported beside the headline only."""
     out = {}
-    for name, flag in (("mbarrier_issuer", "0"), ("named_barrier_issuer", "1")):
-        env = dict(os.environ, HCP_FWD_NAMED_BARRIERS=flag)
+    for name, nb, poly in (("mbarrier_issuer", "0", "0"), ("named_barrier_issuer", "1", "0"),
+                           ("named_barrier_poly_exp2", "1", "1")):
+        env = dict(os.environ, HCP_FWD_NAMED_BARRIERS=nb, HCP_FWD_POLY_EXP2=poly)
         cmd = [sys.executable, os.path.abspath(__file__), "--kernel", "fwd", "--seq", str(seq), "--iters", "5"]
         try:
             r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=180)

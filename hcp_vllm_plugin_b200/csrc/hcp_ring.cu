@@ -87,41 +87,50 @@ bool encode_rows_heads(CUtensorMap* m, bool f16, const void* base, int64_t rows,
 }
 
 std::mutex g_attr_mu;
-bool g_attr_done[2][2][2][64];
+bool g_attr_done[2][2][3][64];
 bool g_dec_attr_done[2][2][64];
 
-// HCP_FWD_NAMED_BARRIERS=1 selects the forward kernel whose MMA issuer meets
-// the softmax warpgroups at named barriers only (read once per process).
-bool fwd_named_barriers() {
-  static const bool on = [] {
-    const char* e = std::getenv("HCP_FWD_NAMED_BARRIERS");
-    return e != nullptr && e[0] == '1';
+// Forward kernel variant (read once per process): HCP_FWD_NAMED_BARRIERS=1
+// selects the MMA issuer that meets the softmax warpgroups at named barriers
+// only (1); HCP_FWD_POLY_EXP2=1 the same with a quarter of the exponentials
+// on the FMA pipe (2); otherwise the mbarrier issuer (0).
+int fwd_variant() {
+  static const int v = [] {
+    auto on = [](const char* name) {
+      const char* e = std::getenv(name);
+      return e != nullptr && e[0] == '1';
+    };
+    return on("HCP_FWD_POLY_EXP2") ? 2 : on("HCP_FWD_NAMED_BARRIERS") ? 1 : 0;
   }();
-  return on;
+  return v;
 }
 
-template <int D, bool F16, bool NB>
+template <int D, bool F16, int V>
 int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
   constexpr int smem = fwd_smem_bytes<D>();
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
-    bool& done = g_attr_done[D == 128][F16][NB][dev];
+    bool& done = g_attr_done[D == 128][F16][V][dev];
     if (!done) {
-      if (cudaFuncSetAttribute(ring_fwd_kernel<D, F16, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      if (cudaFuncSetAttribute(ring_fwd_kernel<D, F16, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem) != cudaSuccess)
         return HCP_ERR_CUDA;
       done = true;
     }
   }
-  ring_fwd_kernel<D, F16, NB><<<grid, kThreads, smem, st>>>(p);
+  ring_fwd_kernel<D, F16, V><<<grid, kThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
 template <int D, bool F16>
 int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
-  return fwd_named_barriers() ? launch_fwd<D, F16, true>(p, grid, st) : launch_fwd<D, F16, false>(p, grid, st);
+  switch (fwd_variant()) {
+    case 1: return launch_fwd<D, F16, 1>(p, grid, st);
+    case 2: return launch_fwd<D, F16, 2>(p, grid, st);
+    default: return launch_fwd<D, F16, 0>(p, grid, st);
+  }
 }
 
 int64_t segment_cost(const hcp_kv_segment& s, int q_len) {

@@ -170,6 +170,29 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x for x <= 0 on the FMA pipe, so part of a tile's exponentials leave the
+// MUFU unit (which two softmax warps per SM sub-partition keep busy for as
+// long as the tensor work of a tile takes).  Cody-Waite reduction
+// x = j + f with j = rint(x) by the 1.5 * 2^23 rounding trick (f in
+// [-1/2, 1/2]); 2^f by a degree-3 polynomial, minimax in relative error on
+// that interval (Remez exchange; coefficients and their 7.5e-5 error from
+// gen_exp2_poly.py); 2^j by adding j to the exponent bits: the low bits of
+// the rounded float hold j, and shifting them by 23 drops the rest.  At or
+// below -126 the result is 0, as ex2.approx.ftz gives for masked keys.
+__device__ __forceinline__ float exp2_poly(float x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992806f, kC1 = 0.69326097f, kC2 = 0.24261113f, kC3 = 0.05517167f;
+  const float xc = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(xc, kMagic);
+  const float f = __fsub_rn(xc, __fsub_rn(t, kMagic));
+  const float p = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
+  const int bits = __float_as_int(p) + (__float_as_int(t) << 23);
+  return x > -126.0f ? __int_as_float(bits) : 0.0f;
+}
+// Pairs of a 16-pair group whose exponentials take the FMA-pipe path
+// (kernel variant 2): one in four.
+__device__ __forceinline__ constexpr bool poly_pair(int i) { return (i & 3) == 3; }
+
 __device__ __forceinline__ float lg2_approx(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -216,12 +239,17 @@ struct FwdSmem {
   static constexpr int kBytes = kEnd + 1024;  // + alignment slack
 };
 
-// NB selects how the MMA issuer synchronises with the softmax warpgroups:
-// false - it waits on mbarriers (P ready, K / V tiles landed);
-// true  - it meets the softmax warpgroups only at named barriers, and they
-//         do the mbarrier waits for the tiles their P feeds (see below).
-template <int D, bool F16, bool NB = false>
+// V selects how the MMA issuer synchronises with the softmax warpgroups and
+// how exponentials are computed:
+// 0 - the issuer waits on mbarriers (P ready, K / V tiles landed);
+// 1 - it meets the softmax warpgroups only at named barriers, and they do the
+//     mbarrier waits for the tiles their P feeds (see below);
+// 2 - as 1, with one in four exponentials of a tile on the FMA pipe
+//     (exp2_poly) instead of the MUFU unit.
+template <int D, bool F16, int V = 0>
 __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_constant__ FwdParams p) {
+  constexpr bool NB = V >= 1;
+  constexpr bool kPoly = V == 2;
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
   using L = FwdSmem<D>;
   constexpr int kHalves = D / 64;
@@ -625,9 +653,11 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
             uint32_t pk[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
-              const float p1 =
-                  ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+              const float x0 = fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base);
+              const float x1 = fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base);
+              const bool fma_pipe = kPoly && poly_pair(i);
+              const float p0 = fma_pipe ? exp2_poly(x0) : ex2_approx(x0);
+              const float p1 = fma_pipe ? exp2_poly(x1) : ex2_approx(x1);
               sums[i & 3] += p0 + p1;
               pk[i] = pack2<F16>(p0, p1);
             }
@@ -639,9 +669,11 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
             uint32_t pk[16], pl[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base));
-              const float p1 =
-                  ex2_approx(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base));
+              const float x0 = fmaf(__uint_as_float(sr[c * 32 + 2 * i]), scale_log2, -m_base);
+              const float x1 = fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), scale_log2, -m_base);
+              const bool fma_pipe = kPoly && poly_pair(i);
+              const float p0 = fma_pipe ? exp2_poly(x0) : ex2_approx(x0);
+              const float p1 = fma_pipe ? exp2_poly(x1) : ex2_approx(x1);
               sums[i & 3] += p0 + p1;
               pk[i] = pack2<F16>(p0, p1);
               const float2 h2 = unpack2<F16>(pk[i]);
