@@ -39,6 +39,11 @@
 // running max is only raised when a tile's max exceeds it by more than 8
 // (P stays <= 2^8) and O is rescaled in TMEM only then.
 // LSE = (m + log2 l) * ln 2.
+//
+// Variants (template parameter V, chosen per process by the host): 0 - the
+// MMA issuer waits on mbarriers; 1 - it meets the softmax warpgroups at
+// named barriers only and they wait on the mbarriers instead; 2 - as 1, with
+// a quarter of the exponentials computed on the FMA pipe (exp2_poly).
 #pragma once
 
 #include <cuda_bf16.h>
