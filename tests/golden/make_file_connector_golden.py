@@ -23,7 +23,7 @@ import types
 import numpy as np
 import torch
 
-REF_ROOT = os.environ.get("HCP_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("HCP_REFERENCE_ROOT", "")  # the reference checkout (generation only)
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "file_connector_case.npz")
 
 LAYERS, HKV, D, BS, NUM_BLOCKS, HEADS = 2, 2, 64, 16, 12, 4
@@ -53,6 +53,8 @@ def write_export(kv_dir: str, kvs: list[torch.Tensor]) -> None:
 
 
 def main() -> None:
+    if not REF_ROOT:
+        raise SystemExit("set HCP_REFERENCE_ROOT to the reference checkout")
     sys.path.insert(0, REF_ROOT)
     from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
     from hcp_vllm_plugin.file_connector import HcpFileConnector  # reference code

@@ -32,7 +32,7 @@ import types
 import numpy as np
 import torch
 
-REF_ROOT = os.environ.get("HCP_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("HCP_REFERENCE_ROOT", "")  # the reference checkout (generation only)
 OUT_DIR = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -197,6 +197,8 @@ def forward_case(rb) -> dict:
 
 
 def main() -> None:
+    if not REF_ROOT:
+        raise SystemExit("set HCP_REFERENCE_ROOT to the reference checkout")
     sys.path.insert(0, REF_ROOT)
     os.environ["HCP_RING_IMPL"] = "torch"
     os.environ["HCP_RING_MERGE"] = "torch"

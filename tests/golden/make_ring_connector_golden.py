@@ -23,7 +23,7 @@ import tempfile
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
-REF_ROOT = os.environ.get("HCP_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("HCP_REFERENCE_ROOT", "")  # the reference checkout (generation only)
 OUT = os.path.join(HERE, "ring_connector_case.json")
 
 BS = 16
@@ -112,6 +112,8 @@ def run(connector_cls, role_scheduler, chunks_and_urls, fake_config) -> dict:
 
 
 def main() -> None:
+    if not REF_ROOT:
+        raise SystemExit("set HCP_REFERENCE_ROOT to the reference checkout")
     sys.path.insert(0, REF_ROOT)
     from vllm.distributed.kv_transfer.kv_connector.v1.base import KVConnectorRole
     from hcp_vllm_plugin import ring_connector as rc  # reference code
