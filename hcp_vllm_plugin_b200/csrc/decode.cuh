@@ -289,12 +289,22 @@ __global__ void __launch_bounds__(kDecThreads) decode_splitkv_kernel(const __gri
       o[j][0] *= alpha;
       o[j][1] *= alpha;
     }
-    // ---- O[16 x D] += P[16 x 16] V[16 x D]
-    uint32_t pa[4];
+    // ---- O[16 x D] += P[16 x 16] V[16 x D], P as a 16-bit high part plus the
+    // 16-bit rest P - hi: two products, so P reaches the accumulator with ~16
+    // significant bits instead of 8 (the extra tensor work is small next to
+    // the K/V bytes this kernel streams).
+    uint32_t pa[4], pl[4];
     pa[0] = pack2<F16>(pr[0][0], pr[0][1]);
     pa[1] = 0;
     pa[2] = pack2<F16>(pr[1][0], pr[1][1]);
     pa[3] = 0;
+    {
+      const float2 h0 = unpack2<F16>(pa[0]), h1 = unpack2<F16>(pa[2]);
+      pl[0] = pack2<F16>(pr[0][0] - h0.x, pr[0][1] - h0.y);
+      pl[1] = 0;
+      pl[2] = pack2<F16>(pr[1][0] - h1.x, pr[1][1] - h1.y);
+      pl[3] = 0;
+    }
 #pragma unroll
     for (int jd = 0; jd < D / 16; ++jd) {
       // matrices: (keys kw0..+7, dims 16jd..+7), (kw0+8.., same), (kw0.., 16jd+8..), (kw0+8.., ...)
@@ -306,6 +316,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_splitkv_kernel(const __gri
       ldsm_x4_t(addr, v0, v1, v2, v3);
       mma16816<F16>(o[2 * jd], pa, v0, v1);
       mma16816<F16>(o[2 * jd + 1], pa, v2, v3);
+      mma16816<F16>(o[2 * jd], pl, v0, v1);
+      mma16816<F16>(o[2 * jd + 1], pl, v2, v3);
     }
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(b_empty(s));

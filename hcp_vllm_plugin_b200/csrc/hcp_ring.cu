@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <vector>
 
 #include "hcp_ring.h"
@@ -676,22 +677,52 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[HCP_DECODE_NOALLOC_SCRATCH_BYTES];
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
+
+CUcontext current_ctx() {
+  CtxGetCurrentFn fn = ctx_get_current_fn();
+  CUcontext c = nullptr;
+  if (fn == nullptr || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};  // device address of the array, per device ordinal
+// Device address of the array in each CUDA context that asked for it.  A
+// device address belongs to one context: a host that makes its own driver
+// context current, or re-creates the primary context, gets a fresh lookup.
+std::vector<std::pair<CUcontext, void*>> g_noalloc_addr;
 
 // The host-side name of the array is not a device address: ask the runtime
-// for it once per device, with that device current.
+// for it once per CUDA context, with that context current.
 int noalloc_scratch_address(void** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
+  void* p = nullptr;
+  CUcontext ctx = current_ctx();
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_decode_noalloc_scratch) != cudaSuccess || p == nullptr)
-      return HCP_ERR_CUDA;
-    g_noalloc_addr[dev] = p;
+  if (ctx != nullptr) {
+    for (const auto& e : g_noalloc_addr)
+      if (e.first == ctx) {
+        *out = e.second;
+        return HCP_OK;
+      }
   }
-  *out = g_noalloc_addr[dev];
+  if (cudaGetSymbolAddress(&p, g_decode_noalloc_scratch) != cudaSuccess || p == nullptr) return HCP_ERR_CUDA;
+  // the lookup may have made the primary context current just now
+  if (ctx == nullptr) ctx = current_ctx();
+  if (ctx != nullptr) g_noalloc_addr.emplace_back(ctx, p);
+  *out = p;
   return HCP_OK;
 }
 

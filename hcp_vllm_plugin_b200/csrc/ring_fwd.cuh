@@ -67,7 +67,7 @@ constexpr int kMaxWork = 160;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
 constexpr float kRescaleThreshold = 8.0f;            // log2 units
-constexpr int kPreciseKeys = 256;  // rows seeing fewer keys get the hi+lo P product
+constexpr int kPreciseKeys = 1024;  // rows seeing fewer keys get the hi+lo P product
 // Named barriers of the NB issuer protocol: event barrier of query tile x
 // (softmax warpgroup x arrives, the MMA warp syncs) and its acknowledgement
 // (the MMA warp arrives, the warpgroup syncs); 128 + 32 threads each.

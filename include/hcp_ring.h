@@ -250,9 +250,9 @@ int hcp_kv_cache_gather(const void* kv_cache, int64_t num_blocks, int32_t block_
  *  - a call whose partials need more than HCP_DECODE_NOALLOC_SCRATCH_BYTES
  *    (hcp_decode_workspace_bytes(args)) returns HCP_ERR_SCRATCH_LIMIT and
  *    launches nothing; a larger args->chunk_keys needs fewer partials;
- *  - the first call on a device looks up the array's device address (once
- *    per device, with that device current); make that first call before
- *    any stream capture begins;
+ *  - the first call in a CUDA context looks up the array's device address
+ *    in that context (once per context, with it current); make that first
+ *    call before any stream capture begins;
  *  - all calls share the one array and it keeps the last call's contents;
  *    nothing in it has to start at zero (each call writes every partial it
  *    reads), but calls that overlap on the GPU (other streams, other host

@@ -17,6 +17,7 @@ import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
+import parity as P  # noqa: E402  (this script's directory is on sys.path)
 from oracle import ring_oracle as ro  # noqa: E402
 
 H, HKV, D, LAYERS, BS = 28, 4, 128, 2, 16
@@ -90,10 +91,12 @@ def main():
                 vals = torch.cat([peer[layer][1], own[r][layer][1]] + [tok[j][r][layer][2] for j in range(t + 1)])
                 want, _ = ro.attn_with_lse(qq[r:r + 1].float().numpy(), keys.float().numpy(),
                                            vals.float().numpy(), D ** -0.5, None)
-                err = np.abs(got[r] - want[0])
-                ok = ok and bool(np.all(err <= 2e-3 + 2.0 ** -7 * np.abs(want[0])))
-                e = float(err.max())
-                worst = max(worst, e if np.isfinite(e) else float("inf"))
+                try:
+                    e = P.check_out(got[r], want[0], f"layer {layer} request {r}").err
+                except AssertionError as ex:
+                    print(ex, flush=True)
+                    ok, e = False, float("inf")
+                worst = max(worst, e)
     ring.stop()
     torch.cuda.synchronize()
     comm.close()

@@ -153,8 +153,11 @@ def test_backend_routes_decode_rows_to_the_ring():
 # GPU: the same routing on the B200 kernels
 # ---------------------------------------------------------------------------
 def _tol_ok(got, want):
-    err = np.abs(got - want)
-    return bool(np.all(err <= 2e-3 + 2.0 ** -7 * np.abs(want))), float(err.max())
+    import parity as P
+    try:
+        return True, P.check_out(np.asarray(got, np.float32), np.asarray(want, np.float32), "decode ring").err
+    except AssertionError as ex:
+        return False, str(ex)
 
 
 @pytest.mark.gpu

@@ -16,6 +16,7 @@ import numpy as np
 import pytest
 import torch
 
+import parity as P
 from oracle import ring_oracle as ro
 
 pytestmark = pytest.mark.gpu
@@ -59,6 +60,5 @@ def _run(C, ops, lib):
     assert C.device_status() == 0
     want, want_lse = ro.attn_with_lse(q.float().cpu().numpy(), k.float().cpu().numpy(),
                                       v.float().cpu().numpy(), d ** -0.5, tk - tq)
-    err = np.abs(out.float().cpu().numpy() - want)
-    assert np.all(err <= 2e-3 + 2.0 ** -7 * np.abs(want))
-    assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-3
+    P.check_out(out.float().cpu().numpy(), want, "forward after a status reset")
+    P.check_lse(lse.cpu().numpy(), want_lse, "forward after a status reset")

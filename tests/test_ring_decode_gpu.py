@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 import torch
 
+import parity as P
 from oracle import ring_oracle as ro
 
 pytestmark = pytest.mark.gpu
@@ -80,18 +81,14 @@ def test_sharded_decode_equals_single_pass():
     ref_lse = torch.empty(H, B, device="cuda")
     ops.decode_splitkv(q, seqs, scale=D ** -0.5, num_kv_heads=HKV, out=ref, lse=ref_lse, peer_k=allk, peer_v=allv)
     torch.cuda.synchronize()
-    # Both paths round P to bf16 against different running maxima (the shards
-    # of request 2 hold one key each, so their P is exactly 1 and the merge is
-    # fp32), so both are held to the decode tolerance against the oracle:
-    # 2e-3 + 2^-7 |ref| on outputs, 1e-3 on LSE.
+    # Both paths are held to the parity bar of tests/parity.py against the oracle.
     for b in range(B):
         kk = torch.cat([shards_k[w][b] for w in range(W)]).float().numpy()
         vv = torch.cat([shards_v[w][b] for w in range(W)]).float().numpy()
         want, want_lse = ro.attn_with_lse(q[b:b + 1].float().cpu().numpy(), kk, vv, D ** -0.5, None)
-        for got, got_lse in ((out, out_lse), (ref, ref_lse)):
-            err = np.abs(got[b].cpu().numpy() - want[0])
-            assert np.all(err <= 2e-3 + 2.0 ** -7 * np.abs(want[0])), (b, err.max())
-            assert np.abs(got_lse[:, b].cpu().numpy() - want_lse[:, 0]).max() < 1e-3
+        for name, got, got_lse in (("ring", out, out_lse), ("one launch", ref, ref_lse)):
+            P.check_out(got[b].float().cpu().numpy(), want[0], f"{name} request {b}")
+            P.check_lse(got_lse[:, b].cpu().numpy(), want_lse[:, 0], f"{name} request {b}")
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
