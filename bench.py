@@ -195,6 +195,8 @@ def main():
     ap.add_argument("--iters", type=int, default=1, help="timed launches in --kernel mode")
     ap.add_argument("--rows", action="store_true",
                     help="measure the connector / decode-ring rows instead of the headline")
+    ap.add_argument("--ref-gpu", action="store_true",
+                    help="time the reference plugin's own B200 path beside this library and exit")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -210,6 +212,12 @@ def main():
         return
     if args.rows:
         run_rows(args, world, rank, local_rank)
+        return
+    if args.ref_gpu:
+        import torch
+        dev = torch.device("cuda", local_rank)
+        torch.cuda.set_device(dev)
+        print(json.dumps({"reference_b200": reference_gpu_side(dev, peaks()[0])}), flush=True)
         return
 
     import datetime
@@ -424,6 +432,167 @@ def side_configs(dev, pk):
         res["fwd_issuer_variants_16k_causal"] = fwd_issuer_variants(16384)
     except Exception as e:  # noqa: BLE001 - reported in the line
         res["fwd_issuer_variants_16k_causal"] = {"error": repr(e)[-300:]}
+    try:
+        res["reference_b200"] = reference_gpu_side(dev, pk)
+    except Exception as e:  # noqa: BLE001 - reported in the line
+        res["reference_b200"] = {"error": repr(e)[-300:]}
+    return res
+
+
+REF_PKG = os.path.join(ROOT, "baseline", "_ref")  # the reference plugin, installed unmodified
+
+
+def reference_gpu_side(dev, pk) -> dict:
+    """The reference plugin's own B200 path, timed beside this library on the
+    same inputs (CUDA events, 3 warm-up calls, so Triton's JIT compile is
+    outside the timed region):
+
+    * ``fwd_16k_causal``: its Triton ``ring_attn_with_lse``
+      (``ring_triton_attn.py:155-207``) on one 16384-token causal launch, vs
+      ``hcp_ring_attn_fwd`` on the same q/k/v;
+    * ``cfg0``: BASELINE configs[0] - its local pass + peer pass + vLLM
+      ``merge_attn_states`` (``ring_backend.py:819-832``), vs one fused launch;
+    * ``cfg1_plugin_forward_28_layers``: BASELINE configs[1] through each
+      plugin's ``HcpRingAttentionImpl.forward`` for a 28-layer engine step (one
+      metadata object per step, 28 layers with their own paged caches and
+      staged 1024-token peer chunks per request): the reference's per-request
+      loop (gather, two Triton passes, merge) vs this backend (one host sync
+      per step, one launch per layer).
+
+    The reference is imported unmodified from ``baseline/_ref``."""
+    import types
+
+    import torch
+
+    if not os.path.isdir(os.path.join(REF_PKG, "hcp_vllm_plugin")):
+        return {"unavailable": "reference package not installed under baseline/_ref"}
+    if REF_PKG not in sys.path:
+        sys.path.append(REF_PKG)
+    from hcp_vllm_plugin import ring_backend as ref_rb  # the reference's own code
+    from hcp_vllm_plugin.ring_triton_attn import ring_attn_with_lse as ref_attn
+    from vllm.v1.attention.ops.merge_attn_states import merge_attn_states
+
+    from hcp_vllm_plugin_b200 import _capi as C
+    from hcp_vllm_plugin_b200 import ops
+    from hcp_vllm_plugin_b200 import ring_backend as our_rb
+
+    res: dict = {}
+    scale = D ** -0.5
+    g = torch.Generator(device=dev).manual_seed(41)
+
+    def timed(fn, n=5):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+
+    def pair(name, fl, ref_fn, our_fn, n=5):
+        try:
+            ms_ref = timed(ref_fn, n)
+            ms_our = timed(our_fn, n)
+            res[name] = {"ref_ms": ms_ref, "ours_ms": ms_our, "speedup": ms_ref / ms_our,
+                         "ref_tflops": fl / ms_ref / 1e9, "ours_tflops": fl / ms_our / 1e9}
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            res[name] = {"error": repr(e)[-300:]}
+
+    # ---- one 16384-token causal launch
+    s = 16384
+    q = torch.empty(s, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    k = torch.empty(s, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    v = torch.empty_like(k).normal_(generator=g)
+    out = torch.empty_like(q)
+    work = ops.make_work([(0, s, 0, 0, (C.HCP_SRC_A, 0, s, 0), None)])
+    pair("fwd_16k_causal", 4.0 * D * H * causal_pairs(s),
+         lambda: ref_attn(q, k, v, scale, 0),
+         lambda: ops.ring_attn_fwd(q, work, scale=scale, num_kv_heads=HKV, out=out, k_a=k, v_a=v))
+    del q, k, v, out
+
+    # ---- configs[0]: local 1024 causal + peer 1024 non-causal + merge
+    t = 1024
+    q = torch.empty(t, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    kl, vl, kp, vp = (torch.empty(t, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+                      for _ in range(4))
+    out = torch.empty_like(q)
+
+    def ref_cfg0():
+        o_loc, lse_loc = ref_attn(q, kl, vl, scale, 0)
+        o_peer, lse_peer = ref_attn(q, kp, vp, scale, None)
+        merged = torch.empty_like(o_loc)
+        merge_attn_states(merged, o_peer, lse_peer, o_loc, lse_loc)
+        return merged
+    w0 = ops.make_work([(0, t, 0, 0, (C.HCP_SRC_A, 0, t, -1), (C.HCP_SRC_B, 0, t, 0))])
+    pair("cfg0", 4.0 * D * H * (t * (t + 1) // 2 + t * t), ref_cfg0,
+         lambda: ops.ring_attn_fwd(q, w0, scale=scale, num_kv_heads=HKV, out=out, k_a=kp, v_a=vp,
+                                   k_b=kl, v_b=vl), n=20)
+    del q, kl, vl, kp, vp, out
+
+    # ---- configs[1] through both plugins' forward, a 28-layer step
+    try:
+        lens, peer, bs, layers = [512, 1024, 2048, 3072], 1024, 16, 28
+        nbl = [(peer + L) // bs for L in lens]
+        nb = sum(nbl)
+        perm = torch.randperm(nb, generator=torch.Generator().manual_seed(1)).to(torch.int32)
+        bt = torch.zeros(len(lens), max(nbl), dtype=torch.int32)
+        o = 0
+        for r, n in enumerate(nbl):
+            bt[r, :n] = perm[o:o + n]
+            o += n
+        bt = bt.to(dev)
+        ntok = sum(lens)
+        qsl = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device=dev)
+        seq_lens = torch.tensor([peer + L for L in lens], dtype=torch.int32, device=dev)
+        names = [f"model.layers.{i}.self_attn.attn" for i in range(layers)]
+        caches = [torch.empty(nb, HKV, bs, 2 * D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+                  for _ in names]
+        # the reference's own layout [nb, 2, bs, Hkv, D], same values
+        ref_caches = [c.view(nb, HKV, bs, 2, D).permute(0, 3, 2, 1, 4).contiguous() for c in caches]
+        qs = [torch.empty(ntok, H, D, dtype=torch.bfloat16, device=dev).normal_(generator=g) for _ in names]
+        out = torch.empty(ntok, H, D, dtype=torch.bfloat16, device=dev)
+        for mod in (ref_rb, our_rb):
+            mod.clear_peer_kv()
+        for r in range(len(lens)):
+            ck = f"bench_req{r}"
+            for nm in names:
+                kpr = torch.empty(peer, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+                vpr = torch.empty_like(kpr).normal_(generator=g)
+                ref_rb.stage_peer_kv(ck, nm, kpr, vpr)
+                our_rb.stage_peer_kv(ck, nm, kpr, vpr)
+            fb = int(bt[r, 0])
+            ref_rb.map_request_peer(fb, [ck])
+            our_rb.map_request_peer(fb, [ck])
+        layer_objs = [types.SimpleNamespace(layer_name=nm) for nm in names]
+
+        def meta():  # a fresh metadata object per engine step
+            return types.SimpleNamespace(num_actual_tokens=ntok, query_start_loc=qsl, seq_lens=seq_lens,
+                                         block_table=bt)
+        ref_impl = ref_rb.HcpRingAttentionImpl(H, D, scale, HKV)
+        our_impl = our_rb.HcpRingAttentionImpl(H, D, scale, HKV)
+
+        def ref_step():
+            m = meta()
+            for i in range(layers):
+                ref_impl.forward(layer_objs[i], qs[i], None, None, ref_caches[i], m, out)
+
+        def our_step():
+            m = meta()
+            for i in range(layers):
+                our_impl.forward(layer_objs[i], qs[i], None, None, caches[i], m, out)
+        our_rb.reset_impl_stats()
+        fl = layers * 4.0 * D * H * sum(L * (L + 1) // 2 + peer * L for L in lens)
+        pair("cfg1_plugin_forward_28_layers", fl, ref_step, our_step, n=3)
+        res["cfg1_plugin_forward_28_layers"]["ours_peer_concat"] = our_rb.IMPL_STATS["peer_concat"]
+        res["cfg1_plugin_forward_28_layers"]["ref_impl_stats"] = dict(ref_rb.IMPL_STATS)
+    except Exception as e:  # noqa: BLE001 - reported in the line
+        res["cfg1_plugin_forward_28_layers"] = {"error": repr(e)[-300:]}
+    finally:
+        for mod in (ref_rb, our_rb):
+            mod.clear_peer_kv()
     return res
 
 
