@@ -73,6 +73,53 @@ def plan_balanced(world: int, chunk: int, tile: int = 128, balance: bool = True)
     return RingPlan(world=world, chunk=chunk, tile=tile, give=give)
 
 
+def needs_chunk(plan: RingPlan, x: int, j: int) -> bool:
+    """Does rank ``x`` read chunk ``j``'s K/V (``j != x``)?  Its own rows past
+    the hand-off see every earlier chunk; the rows it computes for its partner
+    ``s`` see chunks ``0..s-1``."""
+    if j == x:
+        return False
+    if j < x and plan.rows_given(x) < plan.chunk:
+        return True
+    owner = plan.helped_owner(x)
+    return owner is not None and j < owner
+
+
+@dataclass(frozen=True)
+class Hop:
+    """One step of the chunk rotation on one rank.  At hop ``h`` rank ``x``
+    sends its chunk to ``x + h`` and receives chunk ``x - h`` (mod world), each
+    only if the receiving rank reads that chunk: every hop is a permutation of
+    the ranks, so no link carries two chunks at once."""
+    hop: int
+    send_to: int | None      # rank that receives this rank's chunk now
+    recv_chunk: int | None   # chunk (= its owner's rank) received now
+    slot: int                # receive buffer slot, -1 when nothing is received
+    own_rows: bool           # this rank's rows past the hand-off attend the chunk
+    helper_rows: bool        # the rows computed for the partner attend it
+
+
+def hop_schedule(plan: RingPlan, x: int, slots: int = 2) -> list[Hop]:
+    """The hops of rank ``x`` that move a chunk (in or out), in hop order;
+    received chunks cycle through ``slots`` receive buffers."""
+    world = plan.world
+    owner = plan.helped_owner(x)
+    hops, n = [], 0
+    for h in range(1, world):
+        j, y = (x - h) % world, (x + h) % world
+        recv = j if needs_chunk(plan, x, j) else None
+        send = y if needs_chunk(plan, y, x) else None
+        if recv is None and send is None:
+            continue
+        slot, own, helper = -1, False, False
+        if recv is not None:
+            slot, n = n % slots, n + 1
+            own = j < x and plan.rows_given(x) < plan.chunk
+            helper = owner is not None and j < owner
+        hops.append(Hop(h, send, recv, slot, own, helper))
+    return hops
+
+
 def ideal_speedup(plan: RingPlan) -> float:
     """Total work over the slowest rank's work (the scaling bound of the plan)."""
     total = plan.world * plan.world / 2.0
