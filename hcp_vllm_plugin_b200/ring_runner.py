@@ -1,35 +1,48 @@
 """In-box ring context-parallel prefill over NVLink (one process per GPU).
 
 Replaces the reference's HTTP peer-KV pull and neighbour accumulate-forward
-(``ring_connector.py:21-32, 777-859``) inside one 8xB200 box: every layer, the
-K/V chunks rotate around the ring over NVLink (NCCL ring all-gather), then
-the peer chunks, now in local HBM, and the resident chunk are attended in
-one launch.  The work plan (``ring_schedule.plan_balanced``) moves query
-rows from heavy to light ranks so 8 ranks stay balanced.
+(``ring_connector.py:21-32, 777-859``) inside one 8xB200 box.  Rank ``x``
+durably owns contiguous chunk ``x`` (its q/k/v); every layer, the earlier
+chunks it reads arrive hop by hop over NVLink while it computes, and only
+the chunks a rank reads are moved.  The work plan
+(``ring_schedule.plan_balanced``) moves query rows from heavy to light ranks
+so 8 ranks stay balanced.
 
-Per layer on rank x (chunk C tokens, ``give`` rows handed to a helper):
-  1. all-gather K and V of this layer; owner -> helper: Q[0:give]
-  2. ONE launch over every row this rank computes, fp32 out + LSE:
-       rows [give, C): peer chunks [0, x) (non-causal) and the own chunk
-                       (causal) in one online softmax - final values;
-       rows [0, give): the own chunk only (causal) - a partial;
-       helper rows:    the partner's Q rows vs its peer chunks [0, s).
-     The host orders CTAs heaviest first, so the long peer CTAs start first
-     and the short causal ones fill the end of the launch (separate launches
-     per part each ended in a partial wave of equally long CTAs).
-  3. helper: send its partial back; owner: merge rows [0, give) with it;
-     rows [give, C) are cast to the output dtype.
-Every rank issues the same collectives in the same order.
+Per layer on rank x (chunk C, ``give`` rows handed to a helper, P ranks):
+
+* caller's stream (lowest priority), at once:
+    own rows [0, C) vs the own chunk, causal  ->  acc_own (fp32 O, LSE)
+* communication (NCCL send/recv on its own stream), per hop h = 1..P-1:
+    send the own chunk's K/V to rank x+h if that rank reads chunk x, and
+    receive chunk x-h into one of two slots if this rank reads it; a slot is
+    refilled only after the launch that read it has finished.  Each hop is a
+    permutation of the ranks, so no link carries two chunks at once.  Before
+    the hops the owner sends Q rows [0, give) to its helper.
+* hop stream (high priority), one launch per received chunk, each merging
+  into the previous one's (O, LSE) in its epilogue (acc_peer):
+    own rows [give, C) vs the chunk when it precedes x, and the rows computed
+    for the partner vs the chunk when it precedes the partner (the first such
+    launch also attends the helper's own chunk for those rows).
+  The high priority lets each hop launch take the SMs first; the causal
+  launch's short CTAs fill the tail of each hop launch.
+* end: the helper returns its partner's partial (O, LSE); the caller's
+  stream merges acc_own with acc_peer for rows [give, C) and acc_own with the
+  returned partial for rows [0, give), writing the output dtype directly.
+
+TMA reads only this GPU's HBM: received chunks sit in local slots.  Every rank
+issues its collectives in the same order (Q rows, hops 1..P-1, partials).
 """
 
 from __future__ import annotations
+
+import contextlib
 
 import torch
 import torch.distributed as dist
 
 from . import _capi as C
 from . import ops
-from .ring_schedule import RingPlan, plan_balanced
+from .ring_schedule import Hop, RingPlan, hop_schedule, plan_balanced
 
 
 def _cuda_attn(q, work, *, scale, num_kv_heads, out, lse, **src):
@@ -48,7 +61,7 @@ class RingPrefill:
 
     def __init__(self, seq_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
                  scale: float, device: torch.device, dtype: torch.dtype = torch.bfloat16,
-                 group=None, balance: bool = True):
+                 group=None, balance: bool = True, slots: int = 2):
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.world = dist.get_world_size(group)
@@ -57,6 +70,8 @@ class RingPrefill:
             self.world, self.rank = 1, 0
         if seq_len % self.world:
             raise ValueError("seq_len must split evenly over the ranks")
+        if slots < 1:
+            raise ValueError("slots must be >= 1")
         self.chunk = seq_len // self.world
         self.H, self.Hkv, self.D = num_heads, num_kv_heads, head_dim
         self.scale = scale
@@ -68,23 +83,44 @@ class RingPrefill:
         self.helper = self.plan.helper_of(x) if self.give else None
         self.owner = self.plan.helped_owner(x)
         self.owner_give = self.plan.rows_given(self.owner) if self.owner is not None else 0
+        self.hops: list[Hop] = hop_schedule(self.plan, x, slots) if self.world > 1 else []
+        recv_hops = [h for h in self.hops if h.recv_chunk is not None]
+        self.own_peer = any(h.own_rows for h in recv_hops)
+        help_hops = [h for h in recv_hops if h.helper_rows]
+        # the first hop launch writes acc_peer without merging, so it must
+        # cover every row group a later hop launch merges into
+        if recv_hops and ((self.own_peer and not recv_hops[0].own_rows)
+                          or (help_hops and not recv_hops[0].helper_rows)):
+            raise RuntimeError(f"ring plan: rank {x}'s first received chunk does not cover all its rows")
         f32 = torch.float32
+        g = self.owner_give
+        self.slot_k: list[torch.Tensor] = []
+        self.slot_v: list[torch.Tensor] = []
         if self.world > 1:
-            self.k_all = torch.empty(self.world * c, num_kv_heads, head_dim, dtype=dtype, device=device)
-            self.v_all = torch.empty_like(self.k_all)
-            # combined rows of the one launch: own chunk rows, then helper rows
-            rows = c + self.owner_give
-            self.q_comb = torch.empty(rows, num_heads, head_dim, dtype=dtype, device=device)
-            self.acc = torch.empty(rows, num_heads, head_dim, dtype=f32, device=device)
-            self.acc_lse = torch.empty(num_heads, rows, dtype=f32, device=device)
-        if self.owner is not None:
-            g = self.owner_give
-            self.q_help = self.q_comb[c:]
-            self.o_help = self.acc[c:]
+            ns = min(slots, len(recv_hops))
+            self.slot_k = [torch.empty(c, num_kv_heads, head_dim, dtype=dtype, device=device) for _ in range(ns)]
+            self.slot_v = [torch.empty_like(t) for t in self.slot_k]
+            self.acc_own = torch.empty(c, num_heads, head_dim, dtype=f32, device=device)
+            self.lse_own = torch.empty(num_heads, c, dtype=f32, device=device)
+            # acc_peer rows: own rows [0, C), then the partner's rows
+            rows = c + g
+            self.acc_peer = torch.empty(rows, num_heads, head_dim, dtype=f32, device=device)
+            self.lse_peer = torch.empty(num_heads, rows, dtype=f32, device=device)
+            self.q_comb = torch.empty(rows, num_heads, head_dim, dtype=dtype, device=device) if g else None
+        if g:
             self.lse_help = torch.empty(num_heads, g, dtype=f32, device=device)
         if self.give:
             self.o_part = torch.empty(self.give, num_heads, head_dim, dtype=f32, device=device)
             self.lse_part = torch.empty(num_heads, self.give, dtype=f32, device=device)
+        self._cuda = device.type == "cuda"
+        if self._cuda and self.world > 1:
+            self.s_hop = torch.cuda.Stream(device, priority=-100)   # clamped to the highest
+            self.s_comm = torch.cuda.Stream(device, priority=-100)
+            self.slot_free = [torch.cuda.Event() for _ in self.slot_k]
+        if self.world > 1:
+            # NCCL wants every rank of a group in its first collective; the
+            # per-hop send/recv calls involve only pairs
+            dist.barrier(group=group)
         self.launches = 0  # kernels of this library launched (for the bench's count)
 
     # ------------------------------------------------------------------ helpers
@@ -93,67 +129,148 @@ class RingPrefill:
                      out=out, lse=lse, **src)
         self.launches += 1
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
-                lse: torch.Tensor | None = None) -> torch.Tensor:
-        """One attention layer.  q [C, H, D], k/v [C, Hkv, D] of this rank's
-        chunk (global positions [x*C, (x+1)*C)); writes out [C, H, D]."""
-        x, c = self.rank, self.chunk
-        A = C.HCP_SRC_A
-        if self.world == 1:
-            self._attn(q, [(0, c, 0, 0, (A, 0, c, 0), None)], out, lse, k_a=k, v_a=v)
-            return out
-        g = self.group
-        give = self.give
-        # 1. this layer's K/V to every rank (NCCL, NVLink); Q rows to the helper
-        hk = dist.all_gather_into_tensor(self.k_all, k, group=g, async_op=True)
-        hv = dist.all_gather_into_tensor(self.v_all, v, group=g, async_op=True)
-        p2p = []
-        if give:
-            p2p.append(dist.P2POp(dist.isend, q[:give], self._peer(self.helper), group=g))
-        if self.owner is not None:
-            p2p.append(dist.P2POp(dist.irecv, self.q_help, self._peer(self.owner), group=g))
-        hq = dist.batch_isend_irecv(p2p) if p2p else []
-        self.q_comb[:c].copy_(q)
-        for h in (hk, hv, *hq):
-            h.wait()
-        # 2. one launch over all rows of this rank
-        own = (A, x * c, c, 0)                      # own chunk, causal
-        items = []
-        if give:
-            items.append((0, give, 0, 0, own, None))
-        if give < c:
-            if x > 0:
-                items.append((give, c - give, 0, give, (A, 0, x * c, -1), (A, x * c, c, give)))
-            else:
-                items.append((give, c - give, 0, give, (A, x * c, c, give), None))
-        if self.owner is not None:
-            items.append((c, self.owner_give, 0, c, (A, 0, self.owner * c, -1), None))
-        self._attn(self.q_comb, items, self.acc, self.acc_lse, k_a=self.k_all, v_a=self.v_all)
-        # 3. helper partial back to its owner; merges and the output cast
-        send = []
-        if self.owner is not None:
-            self.lse_help.copy_(self.acc_lse[:, c:])
-            dst = self._peer(self.owner)
-            send = [dist.P2POp(dist.isend, self.o_help, dst, group=g),
-                    dist.P2POp(dist.isend, self.lse_help, dst, group=g)]
-        recv = []
-        if give:
-            src = self._peer(self.helper)
-            recv = [dist.P2POp(dist.irecv, self.o_part, src, group=g),
-                    dist.P2POp(dist.irecv, self.lse_part, src, group=g)]
-        hs = dist.batch_isend_irecv(send + recv) if (send or recv) else []
-        if give < c:
-            out[give:].copy_(self.acc[give:c])
-            if lse is not None:
-                lse[:, give:].copy_(self.acc_lse[:, give:c])
-        for h in hs:
-            h.wait()
-        if give:
-            o_lse = None if lse is None else lse[:, :give]
-            self.merge_fn(out[:give], self.acc[:give], self.acc_lse[:, :give], self.o_part,
-                          self.lse_part, o_lse)
-            self.launches += 1
-        return out
+    def _merge(self, out, a, la, b, lb, out_lse):
+        self.merge_fn(out, a, la, b, lb, out_lse)
+        self.launches += 1
+
+    @staticmethod
+    def _on(stream):
+        return torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
+
+    @staticmethod
+    def _record(stream):
+        if stream is None:
+            return None
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        return ev
+
+    @staticmethod
+    def _p2p(ops_):
+        return dist.batch_isend_irecv(ops_) if ops_ else []
 
     def _peer(self, r: int) -> int:
         return dist.get_global_rank(self.group, r) if self.group is not None else r
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                lse: torch.Tensor | None = None) -> torch.Tensor:
+        """One attention layer.  q [C, H, D], k/v [C, Hkv, D] (contiguous) of
+        this rank's chunk (global positions [x*C, (x+1)*C)); writes out
+        [C, H, D] (and lse [H, C]) in stream order on the caller's current
+        stream."""
+        x, c = self.rank, self.chunk
+        A, B = C.HCP_SRC_A, C.HCP_SRC_B
+        if self.world == 1:
+            self._attn(q, [(0, c, 0, 0, (A, 0, c, 0), None)], out, lse, k_a=k, v_a=v)
+            return out
+        if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+            raise ValueError("ring prefill: q, k and v must be contiguous (they are sent as they are)")
+        grp = self.group
+        give, g = self.give, self.owner_give
+        s0 = torch.cuda.current_stream(self.device) if self._cuda else None
+        s_hop = self.s_hop if self._cuda else None
+        s_comm = self.s_comm if self._cuda else None
+        if g:
+            self.q_comb[:c].copy_(q)
+        ev_in = self._record(s0)
+        # 1. own rows vs the own chunk, causal: no communication needed
+        self._attn(q, [(0, c, 0, 0, (A, 0, c, 0), None)], self.acc_own, self.lse_own, k_a=k, v_a=v)
+        # 2. communication: Q rows to the helper, then the hops
+        if self._cuda:
+            s_comm.wait_event(ev_in)
+            s_hop.wait_event(ev_in)
+        with self._on(s_comm):
+            q_ops = []
+            if give:
+                q_ops.append(dist.P2POp(dist.isend, q[:give], self._peer(self.helper), group=grp))
+            if g:
+                q_ops.append(dist.P2POp(dist.irecv, self.q_comb[c:], self._peer(self.owner), group=grp))
+            q_works = self._p2p(q_ops)
+        if g:
+            with self._on(s_hop):
+                for w in q_works:
+                    w.wait()
+        send_works = list(q_works) if give else []
+        qsrc = self.q_comb if g else q
+        first = True
+        used = [False] * len(self.slot_k)
+        for hop in self.hops:
+            s = hop.slot
+            with self._on(s_comm):
+                if s >= 0 and used[s] and self._cuda:
+                    s_comm.wait_event(self.slot_free[s])
+                hop_ops = []
+                if hop.send_to is not None:
+                    dst = self._peer(hop.send_to)
+                    hop_ops += [dist.P2POp(dist.isend, k, dst, group=grp),
+                                dist.P2POp(dist.isend, v, dst, group=grp)]
+                if hop.recv_chunk is not None:
+                    src = self._peer(hop.recv_chunk)
+                    hop_ops += [dist.P2POp(dist.irecv, self.slot_k[s], src, group=grp),
+                                dist.P2POp(dist.irecv, self.slot_v[s], src, group=grp)]
+                works = self._p2p(hop_ops)
+            if hop.send_to is not None:
+                send_works += works
+            if hop.recv_chunk is None:
+                continue
+            with self._on(s_hop):
+                for w in works:
+                    w.wait()
+                items = []
+                if hop.own_rows:
+                    items.append((give, c - give, 0, give, (A, 0, c, -1), None))
+                if hop.helper_rows:
+                    # the first launch over the partner's rows also attends this rank's own chunk
+                    items.append((c, g, 0, c, (A, 0, c, -1), (B, 0, c, -1) if first else None))
+                merge = {} if first else {"merge_o": self.acc_peer, "merge_lse": self.lse_peer}
+                self._attn(qsrc, items, self.acc_peer, self.lse_peer, k_a=self.slot_k[s], v_a=self.slot_v[s],
+                           k_b=k, v_b=v, **merge)
+                if self._cuda:
+                    self.slot_free[s].record(s_hop)
+            used[s] = True
+            first = False
+        if g and first:
+            # a helper that receives nothing: the partner's rows see only this chunk
+            with self._on(s_hop):
+                self._attn(qsrc, [(c, g, 0, c, (A, 0, c, -1), None)], self.acc_peer, self.lse_peer,
+                           k_a=k, v_a=v)
+        # 3. partials back to the owners
+        ret_works = []
+        if g:
+            with self._on(s_hop):
+                self.lse_help.copy_(self.lse_peer[:, c:])
+            ev_help = self._record(s_hop)
+            with self._on(s_comm):
+                if self._cuda:
+                    s_comm.wait_event(ev_help)
+                dst = self._peer(self.owner)
+                send_works += self._p2p([dist.P2POp(dist.isend, self.acc_peer[c:], dst, group=grp),
+                                         dist.P2POp(dist.isend, self.lse_help, dst, group=grp)])
+        if give:
+            with self._on(s_comm):
+                src = self._peer(self.helper)
+                ret_works = self._p2p([dist.P2POp(dist.irecv, self.o_part, src, group=grp),
+                                       dist.P2POp(dist.irecv, self.lse_part, src, group=grp)])
+        # 4. the caller's stream: wait for the hops, merge, write the output dtype
+        if self._cuda:
+            s0.wait_stream(s_hop)
+        if give < c:
+            o_lse = None if lse is None else lse[:, give:]
+            if self.own_peer:
+                self._merge(out[give:], self.acc_own[give:], self.lse_own[:, give:], self.acc_peer[give:c],
+                            self.lse_peer[:, give:c], o_lse)
+            else:
+                out[give:].copy_(self.acc_own[give:])
+                if o_lse is not None:
+                    o_lse.copy_(self.lse_own[:, give:])
+        if give:
+            for w in ret_works:
+                w.wait()
+            o_lse = None if lse is None else lse[:, :give]
+            self._merge(out[:give], self.acc_own[:give], self.lse_own[:, :give], self.o_part, self.lse_part,
+                        o_lse)
+        # the caller may overwrite q/k/v once this returns: wait for the sends
+        for w in send_works:
+            w.wait()
+        return out
