@@ -210,9 +210,12 @@ class RingPrefill:
                     hop_ops += [dist.P2POp(dist.irecv, self.slot_k[s], src, group=grp),
                                 dist.P2POp(dist.irecv, self.slot_v[s], src, group=grp)]
                 works = self._p2p(hop_ops)
-            if hop.send_to is not None:
-                send_works += works
             if hop.recv_chunk is None:
+                # only sends: waited for at the end.  A hop that also receives
+                # is waited for on the hop stream below, which the caller's
+                # stream waits for (a work is waited for once: gloo blocks on
+                # a second wait)
+                send_works += works
                 continue
             with self._on(s_hop):
                 for w in works:

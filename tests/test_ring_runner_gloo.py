@@ -85,7 +85,7 @@ def _worker(rank, world, port, seq, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,seq", [(2, 512), (3, 768), (4, 1024)])
+@pytest.mark.parametrize("world,seq", [(2, 512), (3, 768), (4, 1024), (5, 1280), (8, 2048)])
 def test_ring_prefill_schedule_gloo(world, seq):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
