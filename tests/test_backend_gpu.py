@@ -80,8 +80,7 @@ def test_backend_forward_matches_reference_forward():
                          block_table=z["block_table"], query_start_loc=z["query_start_loc"],
                          seq_lens=z["seq_lens"], scale=scale, staged=staged)
     want = ro.ring_forward(batch, round_to_bf16=False)
-    np.testing.assert_array_equal(P.round_to(want, torch.bfloat16), ref_out)
-    print(P.check_out(got, want, "backend forward vs reference forward").line())
+    print(P.check_out(got, want, "backend forward vs reference forward", ref_out=ref_out).line())
     assert (out[ntok:].float() == 0).all()  # padding rows untouched
 
 
