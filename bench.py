@@ -231,8 +231,12 @@ def main():
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
+        # NCCL on high-priority streams: a chunk's send/recv kernels take the
+        # first free SM instead of queueing behind attention CTAs
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
+                                device_id=dev, pg_options=opts)
     _capi.load()
     seq, L = args.seq, args.layers
     chunk = seq // world
