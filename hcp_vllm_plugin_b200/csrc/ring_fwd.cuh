@@ -64,6 +64,9 @@ constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
 constexpr int kThreads = 320;
 constexpr int kMaxWork = 160;
+constexpr int kMaxSegs = 2 * kMaxWork;   // segments of one launch's work items
+constexpr int kMaxItemSegs = HCP_MAX_ITEM_SEGMENTS;
+constexpr int kMaxExt = HCP_MAX_EXT_SOURCES;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;  // 4 s
 constexpr float kRescaleThreshold = 8.0f;            // log2 units
@@ -84,6 +87,17 @@ enum : int {
   kErrWaitSelftest = 0x1ff,
 };
 
+// One work item as the kernel sees it: its segments are segs[seg_first ..
+// seg_first + seg_count).
+struct FwdItem {
+  int q_start;
+  int q_len;
+  int paged_req;
+  int lse_col;
+  int seg_first;
+  int seg_count;
+};
+
 struct FwdParams {
   CUtensorMap tm_q;      // {D, H, q_rows}     box {64, 1, 128}
   CUtensorMap tm_ka;     // {D, Hkv, rows_a}   box {64, 1, 128}
@@ -91,6 +105,8 @@ struct FwdParams {
   CUtensorMap tm_kb;
   CUtensorMap tm_vb;
   CUtensorMap tm_cache;  // {2D, bs, Hkv, nb}  box {64, bs, 1, 1}
+  CUtensorMap tm_ek[kMaxExt];  // extra contiguous sources (HCP_SRC_EXT0 + i)
+  CUtensorMap tm_ev[kMaxExt];
   const int32_t* block_table;
   long long bt_stride;
   long long bt_rows;
@@ -112,7 +128,8 @@ struct FwdParams {
   float scale_log2;
   int total_tiles;
   int tile_off[kMaxWork + 1];
-  hcp_attn_work work[kMaxWork];
+  FwdItem work[kMaxWork];
+  hcp_kv_segment segs[kMaxSegs];
 };
 
 // Bounded mbarrier wait.  Returns false when this CTA aborted (this wait ran
@@ -240,7 +257,12 @@ struct FwdSmem {
   static constexpr int kNumBars = 8 + 4 * kStages;
   static constexpr int kKvOff = 2 * kTileBytes;                    // after Q_A, Q_B
   static constexpr int kBarOff = kKvOff + 2 * kStages * kTileBytes;
-  static constexpr int kEnd = kBarOff + 8 * kNumBars + 16;
+  // after the barriers: TMEM slot + abort flag (16 B), then the CTA's
+  // segment table: tile prefix [kMaxItemSegs + 1], keys needed by query tile
+  // A and by B [kMaxItemSegs] each, segment count, precise flags A and B
+  static constexpr int kSegOff = kBarOff + 8 * kNumBars + 16;
+  static constexpr int kSegInts = (kMaxItemSegs + 1) + 2 * kMaxItemSegs + 3;
+  static constexpr int kEnd = kSegOff + 4 * kSegInts;
   static constexpr int kBytes = kEnd + 1024;  // + alignment slack
 };
 
@@ -295,32 +317,40 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     const int mid = (lo + hi + 1) >> 1;
     if (p.tile_off[mid] <= tile_global) lo = mid; else hi = mid - 1;
   }
-  const hcp_attn_work& wk = p.work[lo];
+  const FwdItem& wk = p.work[lo];
+  const hcp_kv_segment* segs = p.segs + wk.seg_first;
   const int n_blocks = (wk.q_len + kCtaRows - 1) / kCtaRows;
   const int m_blk = n_blocks - 1 - (tile_global - p.tile_off[lo]);  // heaviest (last) first
   const int q0 = m_blk * kCtaRows;
   const int rows_a = max(0, min(kBlockM, wk.q_len - q0));
   const int rows_b = max(0, min(kBlockM, wk.q_len - q0 - kBlockM));
-  // keys each query tile needs from each segment; the KV tile list covers both
-  const int ka0 = segment_keys(wk.seg[0], q0, rows_a), kb0 = segment_keys(wk.seg[0], q0 + kBlockM, rows_b);
-  const int ka1 = segment_keys(wk.seg[1], q0, rows_a), kb1 = segment_keys(wk.seg[1], q0 + kBlockM, rows_b);
-  const int tiles0 = (max(ka0, kb0) + kBlockN - 1) / kBlockN;
-  const int n_tiles = tiles0 + (max(ka1, kb1) + kBlockN - 1) / kBlockN;
-  auto tile_seg = [&](int t) { return t < tiles0 ? 0 : 1; };
-  auto tile_key0 = [&](int t) { return (t < tiles0 ? t : t - tiles0) * kBlockN; };
-  // is KV tile t needed by query tile x (0 = A, 1 = B)?
-  auto active = [&](int x, int t) {
-    const int k0 = tile_key0(t);
-    const int need = tile_seg(t) == 0 ? (x == 0 ? ka0 : kb0) : (x == 0 ? ka1 : kb1);
-    return k0 < need;
-  };
-  // Rows that see few keys in total get P as hi + lo 16-bit parts.
-  const bool precise_a = segment_keys(wk.seg[0], q0, 1) + segment_keys(wk.seg[1], q0, 1) < kPreciseKeys;
-  const bool precise_b = segment_keys(wk.seg[0], q0 + kBlockM, 1) +
-                             segment_keys(wk.seg[1], q0 + kBlockM, 1) < kPreciseKeys;
+  // The CTA's segment table (shared memory, filled by thread 0 at setup):
+  // the KV tiles of segment s are [sg_base[s], sg_base[s+1]); query tile A
+  // needs its first sg_need_a[s] keys, B its first sg_need_b[s].
+  int* sg_base = reinterpret_cast<int*>(smem + L::kSegOff);
+  int* sg_need_a = sg_base + kMaxItemSegs + 1;
+  int* sg_need_b = sg_need_a + kMaxItemSegs;
+  int* sg_misc = sg_need_b + kMaxItemSegs;  // [0] segments, [1] precise A, [2] precise B
 
   // ---- setup
   if (threadIdx.x == 0) {
+    // keys each query tile needs from each segment; the KV tile list covers both
+    int tiles = 0, keys_a = 0, keys_b = 0;
+    const int n_seg = min(wk.seg_count, kMaxItemSegs);
+    for (int s = 0; s < n_seg; ++s) {
+      const int ka = segment_keys(segs[s], q0, rows_a), kb = segment_keys(segs[s], q0 + kBlockM, rows_b);
+      sg_base[s] = tiles;
+      sg_need_a[s] = ka;
+      sg_need_b[s] = kb;
+      tiles += (max(ka, kb) + kBlockN - 1) / kBlockN;
+      keys_a += segment_keys(segs[s], q0, 1);
+      keys_b += segment_keys(segs[s], q0 + kBlockM, 1);
+    }
+    sg_base[n_seg] = tiles;
+    sg_misc[0] = n_seg;
+    // Rows that see few keys in total get P as hi + lo 16-bit parts.
+    sg_misc[1] = keys_a < kPreciseKeys;
+    sg_misc[2] = keys_b < kPreciseKeys;
     ptx::mbar_init(b_q, 1);
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(b_kfull(s), 1);
@@ -352,6 +382,20 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int n_seg = sg_misc[0];
+  const int n_tiles = sg_base[n_seg];
+  const bool precise_a = sg_misc[1] != 0, precise_b = sg_misc[2] != 0;
+  auto tile_seg = [&](int t) {
+    int s = 0;
+    while (s + 1 < n_seg && t >= sg_base[s + 1]) ++s;
+    return s;
+  };
+  auto tile_key0 = [&](int t) { return (t - sg_base[tile_seg(t)]) * kBlockN; };
+  // is KV tile t needed by query tile x (0 = A, 1 = B)?
+  auto active = [&](int x, int t) {
+    const int s = tile_seg(t);
+    return (t - sg_base[s]) * kBlockN < (x == 0 ? sg_need_a[s] : sg_need_b[s]);
+  };
   const bool skip_all = *abort_flag != 0;
 
   if (skip_all) {
@@ -370,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       const int s = t % kStages;
       const uint32_t ph = (t / kStages) & 1;
       const int key0 = tile_key0(t);
-      const hcp_kv_segment& seg = wk.seg[tile_seg(t)];
+      const hcp_kv_segment& seg = segs[tile_seg(t)];
       const uint32_t s_k = s_kv0 + (2 * s) * kTileBytes;
       const uint32_t s_v = s_k + kTileBytes;
       int blk_ids[8];
@@ -400,7 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
               ptx::tma_load_4d(s_k + hf * kBoxBytes + i * bs * 128, &p.tm_cache, b_kfull(s), hf * 64,
                                0, kvh, blk_ids[i]);
         } else {
-          const CUtensorMap* tk = seg.src == HCP_SRC_A ? &p.tm_ka : &p.tm_kb;
+          const CUtensorMap* tk = seg.src == HCP_SRC_A   ? &p.tm_ka
+                                  : seg.src == HCP_SRC_B ? &p.tm_kb
+                                                         : &p.tm_ek[seg.src - HCP_SRC_EXT0];
           for (int hf = 0; hf < kHalves; ++hf)
             ptx::tma_load_3d(s_k + hf * kBoxBytes, tk, b_kfull(s), hf * 64, kvh, seg.start + key0);
         }
@@ -416,7 +462,9 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
               ptx::tma_load_4d(s_v + hf * kBoxBytes + i * bs * 128, &p.tm_cache, b_vfull(s),
                                D + hf * 64, 0, kvh, blk_ids[i]);
         } else {
-          const CUtensorMap* tv = seg.src == HCP_SRC_A ? &p.tm_va : &p.tm_vb;
+          const CUtensorMap* tv = seg.src == HCP_SRC_A   ? &p.tm_va
+                                  : seg.src == HCP_SRC_B ? &p.tm_vb
+                                                         : &p.tm_ev[seg.src - HCP_SRC_EXT0];
           for (int hf = 0; hf < kHalves; ++hf)
             ptx::tma_load_3d(s_v + hf * kBoxBytes, tv, b_vfull(s), hf * 64, kvh, seg.start + key0);
         }
@@ -624,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       if (ok) {
         ptx::tc_fence_after();
         const int key0 = tile_key0(t);
-        const hcp_kv_segment& seg = wk.seg[tile_seg(t)];
+        const hcp_kv_segment& seg = segs[tile_seg(t)];
         int vis = seg.len - key0;
         if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
         vis = max(0, min(vis, kBlockN));
@@ -741,7 +789,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       if (!ok) break;
       ptx::tc_fence_after();
       const int key0 = tile_key0(t);
-      const hcp_kv_segment& seg = wk.seg[tile_seg(t)];
+      const hcp_kv_segment& seg = segs[tile_seg(t)];
       int vis = seg.len - key0;
       if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
       vis = max(0, min(vis, kBlockN));

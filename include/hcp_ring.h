@@ -37,15 +37,34 @@ typedef enum hcp_status {
 
 typedef enum hcp_dtype { HCP_BF16 = 0, HCP_F16 = 1, HCP_F32 = 2 } hcp_dtype;
 
+/* Limits of the segment lists and extra sources below. */
+#define HCP_MAX_ITEM_SEGMENTS 8
+#define HCP_MAX_EXT_SOURCES 8
+
 /* Where the keys of one KV segment come from. */
 typedef enum hcp_kv_src {
   HCP_SRC_NONE = 0,   /* segment unused */
   HCP_SRC_A = 1,      /* contiguous k_a / v_a rows [start, start+len) */
   HCP_SRC_B = 2,      /* contiguous k_b / v_b rows [start, start+len) */
-  HCP_SRC_PAGED = 3   /* paged cache: key positions [start, start+len) of the
+  HCP_SRC_PAGED = 3,  /* paged cache: key positions [start, start+len) of the
                          sequence in block_table row `paged_req`; start must be
                          a multiple of block_size */
+  HCP_SRC_LIST = 4,   /* only in a work item's seg[0] (seg[1] unused): the
+                         item's segments are seg_list[start, start+len),
+                         at most HCP_MAX_ITEM_SEGMENTS of them */
+  HCP_SRC_EXT0 = 16   /* HCP_SRC_EXT0 + i: contiguous rows [start, start+len)
+                         of extra source ext[i], i < HCP_MAX_EXT_SOURCES */
 } hcp_kv_src;
+
+/* A contiguous K/V source: k and v [rows, Hkv, D], row stride in elements
+ * (the same for k and v).  Staged peer chunks are passed as they lie, so
+ * several chunks or requests need no concatenation. */
+typedef struct hcp_kv_source {
+  const void* k;
+  const void* v;
+  int64_t rows;
+  int64_t row_stride;
+} hcp_kv_source;
 
 /* One KV segment of a work item.  causal_off < 0: non-causal (every key
  * visible).  causal_off >= 0: key j (segment-relative) is visible to query row
@@ -92,12 +111,19 @@ typedef struct hcp_fwd_args {
   const hcp_attn_work* work;  /* HOST array of num_work items */
   int32_t num_work;
   int32_t _pad4;
+  /* Optional: extra contiguous sources (HOST array, <= HCP_MAX_EXT_SOURCES)
+   * and the segment lists of HCP_SRC_LIST items (HOST array).  NULL / 0
+   * when unused. */
+  const hcp_kv_source* ext;   int32_t num_ext;     int32_t _pad5;
+  const hcp_kv_segment* seg_list; int32_t num_seg_list; int32_t _pad6;
 } hcp_fwd_args;
 
 /*
- * Fused ring-attention forward: flash attention with per-row LSE over up to
- * two KV segments per work item (GQA, global-offset causal mask, paged or
- * contiguous keys), optional merge into an earlier partial (O, LSE).
+ * Fused ring-attention forward: flash attention with per-row LSE over the
+ * KV segments of each work item - two inline, or a list of up to
+ * HCP_MAX_ITEM_SEGMENTS (GQA, global-offset causal mask, paged or contiguous
+ * keys, several contiguous sources) - in one online softmax per row, optional
+ * merge into an earlier partial (O, LSE).
  * tcgen05 MMA with TMEM accumulators, TMA-staged tiles.
  *
  * Replaces, in the reference:
@@ -107,6 +133,9 @@ typedef struct hcp_fwd_args {
  *   peer pass, merge)            hcp_vllm_plugin/ring_backend.py:611-832
  *   _merge / merge_attn_states on the prefill path
  *                                hcp_vllm_plugin/ring_backend.py:339-360
+ *   the concatenation of ordered staged prefix chunks (and of several
+ *   requests' peers) into one peer segment
+ *                                hcp_vllm_plugin/ring_backend.py:751-772
  */
 int hcp_ring_attn_fwd(const hcp_fwd_args* args, void* stream);
 
