@@ -23,7 +23,19 @@ STATUS_NAMES = {
 }
 
 HCP_BF16, HCP_F16, HCP_F32 = 0, 1, 2
-HCP_SRC_NONE, HCP_SRC_A, HCP_SRC_B, HCP_SRC_PAGED = 0, 1, 2, 3
+HCP_SRC_NONE, HCP_SRC_A, HCP_SRC_B, HCP_SRC_PAGED, HCP_SRC_LIST = 0, 1, 2, 3, 4
+HCP_SRC_EXT0 = 16          # HCP_SRC_EXT0 + i: extra contiguous source i
+HCP_MAX_ITEM_SEGMENTS = 8  # segments in one work item's list
+HCP_MAX_EXT_SOURCES = 8    # extra contiguous sources per call
+
+
+class HcpKvSource(ctypes.Structure):
+    _fields_ = [
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("row_stride", ctypes.c_int64),
+    ]
 
 
 class HcpKvSegment(ctypes.Structure):
@@ -70,6 +82,9 @@ class HcpFwdArgs(ctypes.Structure):
         ("merge_lse", ctypes.c_void_p), ("merge_lse_stride", ctypes.c_int64),
         ("work", ctypes.POINTER(HcpAttnWork)), ("num_work", ctypes.c_int32),
         ("_pad4", ctypes.c_int32),
+        ("ext", ctypes.POINTER(HcpKvSource)), ("num_ext", ctypes.c_int32), ("_pad5", ctypes.c_int32),
+        ("seg_list", ctypes.POINTER(HcpKvSegment)), ("num_seg_list", ctypes.c_int32),
+        ("_pad6", ctypes.c_int32),
     ]
 
 
@@ -105,6 +120,8 @@ class HcpDecodeArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_int64),
         ("seqs", ctypes.POINTER(HcpDecodeSeq)), ("num_seqs", ctypes.c_int32),
         ("_pad2", ctypes.c_int32),
+        ("ext", ctypes.POINTER(HcpKvSource)), ("num_ext", ctypes.c_int32), ("_pad3", ctypes.c_int32),
+        ("peer_src", ctypes.POINTER(ctypes.c_int32)),
     ]
 
 

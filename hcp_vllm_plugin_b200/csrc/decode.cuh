@@ -40,12 +40,15 @@ struct DecodeSeq {
   int paged_req;
   int local_start;
   int local_len;
+  int peer_src;  // -1: the peer arena (tm_pk / tm_pv); i: extra source i
 };
 
 struct DecodeParams {
   CUtensorMap tm_pk;     // peer K {D, Hkv, rows}   box {64, 1, 64}
   CUtensorMap tm_pv;     // peer V
   CUtensorMap tm_cache;  // {2D, bs, Hkv, nb}       box {64, bs, 1, 1}
+  CUtensorMap tm_epk[HCP_MAX_EXT_SOURCES];  // extra peer sources, as tm_pk / tm_pv
+  CUtensorMap tm_epv[HCP_MAX_EXT_SOURCES];
   const void* q;
   long long q_row_stride;
   const int32_t* block_table;
@@ -187,9 +190,11 @@ __global__ void __launch_bounds__(kDecThreads) decode_splitkv_kernel(const __gri
         const uint32_t sv = sk + L::kTileBytes;
         ptx::mbar_arrive_expect_tx(b_full(s), L::kStageBytes);
         if (is_peer) {
+          const CUtensorMap* tpk = sq.peer_src < 0 ? &p.tm_pk : &p.tm_epk[sq.peer_src];
+          const CUtensorMap* tpv = sq.peer_src < 0 ? &p.tm_pv : &p.tm_epv[sq.peer_src];
           for (int hf = 0; hf < kHalves; ++hf) {
-            ptx::tma_load_3d(sk + hf * L::kHalfBytes, &p.tm_pk, b_full(s), hf * 64, kvh, sq.peer_start + k0);
-            ptx::tma_load_3d(sv + hf * L::kHalfBytes, &p.tm_pv, b_full(s), hf * 64, kvh, sq.peer_start + k0);
+            ptx::tma_load_3d(sk + hf * L::kHalfBytes, tpk, b_full(s), hf * 64, kvh, sq.peer_start + k0);
+            ptx::tma_load_3d(sv + hf * L::kHalfBytes, tpv, b_full(s), hf * 64, kvh, sq.peer_start + k0);
           }
         } else {
           for (int i = 0; i < nblk; ++i)

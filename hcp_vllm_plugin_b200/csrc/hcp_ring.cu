@@ -163,6 +163,11 @@ int validate_segment(const hcp_fwd_args* a, const hcp_attn_work& w, const hcp_kv
         return HCP_ERR_INVALID;
       return HCP_OK;
     default:
+      if (s.src >= HCP_SRC_EXT0 && s.src < HCP_SRC_EXT0 + a->num_ext) {
+        const hcp_kv_source& e = a->ext[s.src - HCP_SRC_EXT0];
+        if (static_cast<int64_t>(s.start) + s.len > e.rows) return HCP_ERR_INVALID;
+        return HCP_OK;
+      }
       return HCP_ERR_INVALID;
   }
 }
@@ -255,12 +260,33 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
       return HCP_ERR_INVALID;
   }
 
-  // Validate and order the work: most expensive items first.
+  if (a->num_ext < 0 || a->num_ext > HCP_MAX_EXT_SOURCES || (a->num_ext > 0 && a->ext == nullptr) ||
+      a->num_seg_list < 0 || (a->num_seg_list > 0 && a->seg_list == nullptr))
+    return HCP_ERR_INVALID;
+  for (int i = 0; i < a->num_ext; ++i) {
+    const hcp_kv_source& e = a->ext[i];
+    if (e.k == nullptr || e.v == nullptr || e.rows <= 0 || e.row_stride < kv_row || (e.row_stride % 8) != 0 ||
+        !aligned16(e.k) || !aligned16(e.v))
+      return HCP_ERR_INVALID;
+  }
+
+  // Validate and order the work: most expensive items first.  Each item is
+  // kept with its segments (the two inline ones, or its list).
   std::vector<hcp_attn_work> items;
+  std::vector<std::vector<hcp_kv_segment>> item_segs;
   items.reserve(a->num_work);
   std::vector<int64_t> cost;
   for (int i = 0; i < a->num_work; ++i) {
     const hcp_attn_work& w = a->work[i];
+    std::vector<hcp_kv_segment> sg;
+    if (w.seg[0].src == HCP_SRC_LIST) {
+      if (w.seg[1].src != HCP_SRC_NONE || w.seg[0].start < 0 || w.seg[0].len < 0 ||
+          w.seg[0].len > HCP_MAX_ITEM_SEGMENTS || static_cast<int64_t>(w.seg[0].start) + w.seg[0].len > a->num_seg_list)
+        return HCP_ERR_INVALID;
+      sg.assign(a->seg_list + w.seg[0].start, a->seg_list + w.seg[0].start + w.seg[0].len);
+    } else {
+      sg.assign(w.seg, w.seg + 2);
+    }
     if (w.q_len < 0 || w.q_start < 0 || static_cast<int64_t>(w.q_start) + w.q_len > a->q_rows)
       return HCP_ERR_INVALID;
     if (a->lse != nullptr && (w.lse_col < 0 || static_cast<int64_t>(w.lse_col) + w.q_len > a->lse_stride))
@@ -268,19 +294,22 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
     if (a->merge_lse != nullptr &&
         (w.lse_col < 0 || static_cast<int64_t>(w.lse_col) + w.q_len > a->merge_lse_stride))
       return HCP_ERR_INVALID;
-    for (int s = 0; s < 2; ++s) {
-      const int rc = validate_segment(a, w, w.seg[s]);
+    for (const hcp_kv_segment& sgi : sg) {
+      if (sgi.src == HCP_SRC_LIST) return HCP_ERR_INVALID;
+      const int rc = validate_segment(a, w, sgi);
       if (rc != HCP_OK) return rc;
     }
     if (w.q_len == 0) continue;
     items.push_back(w);
+    item_segs.push_back(std::move(sg));
   }
   if (items.empty()) return HCP_OK;
   std::vector<int> order(items.size());
   for (size_t i = 0; i < items.size(); ++i) {
     order[i] = static_cast<int>(i);
-    cost.push_back(segment_cost(items[i].seg[0], items[i].q_len) +
-                   segment_cost(items[i].seg[1], items[i].q_len));
+    int64_t c = 0;
+    for (const hcp_kv_segment& sgi : item_segs[i]) c += segment_cost(sgi, items[i].q_len);
+    cost.push_back(c);
   }
   std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return cost[x] > cost[y]; });
 
@@ -294,6 +323,13 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
   if (want_b && (!encode_rows_heads(&p.tm_kb, f16, a->k_b, a->rows_b, Hkv, D, a->b_row_stride) ||
                  !encode_rows_heads(&p.tm_vb, f16, a->v_b, a->rows_b, Hkv, D, a->b_row_stride)))
     return HCP_ERR_CUDA;
+  for (int i = 0; i < kMaxExt; ++i) p.tm_ek[i] = p.tm_ev[i] = p.tm_q;
+  for (int i = 0; i < a->num_ext; ++i) {
+    const hcp_kv_source& e = a->ext[i];
+    if (!encode_rows_heads(&p.tm_ek[i], f16, e.k, e.rows, Hkv, D, e.row_stride) ||
+        !encode_rows_heads(&p.tm_ev[i], f16, e.v, e.rows, Hkv, D, e.row_stride))
+      return HCP_ERR_CUDA;
+  }
   if (want_paged) {
     const uint64_t bs = static_cast<uint64_t>(a->block_size);
     const uint64_t dims[4] = {static_cast<uint64_t>(2 * D), bs, static_cast<uint64_t>(Hkv),
@@ -323,14 +359,27 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
   p.scale_log2 = a->scale * 1.4426950408889634f;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  for (size_t base = 0; base < order.size(); base += kMaxWork) {
-    const int n = static_cast<int>(std::min<size_t>(kMaxWork, order.size() - base));
-    int tiles = 0;
-    for (int i = 0; i < n; ++i) {
-      p.work[i] = items[order[base + i]];
-      p.tile_off[i] = tiles;
-      tiles += (p.work[i].q_len + kCtaRows - 1) / kCtaRows;
+  for (size_t base = 0; base < order.size();) {
+    // one launch: up to kMaxWork items whose segments fit kMaxSegs
+    int n = 0, nseg = 0, tiles = 0;
+    while (base + n < order.size() && n < kMaxWork) {
+      const int idx = order[base + n];
+      const auto& sg = item_segs[idx];
+      if (nseg + static_cast<int>(sg.size()) > kMaxSegs) break;
+      const hcp_attn_work& w = items[idx];
+      FwdItem& it = p.work[n];
+      it.q_start = w.q_start;
+      it.q_len = w.q_len;
+      it.paged_req = w.paged_req;
+      it.lse_col = w.lse_col;
+      it.seg_first = nseg;
+      it.seg_count = static_cast<int>(sg.size());
+      for (const hcp_kv_segment& sgi : sg) p.segs[nseg++] = sgi;
+      p.tile_off[n] = tiles;
+      tiles += (w.q_len + kCtaRows - 1) / kCtaRows;
+      ++n;
     }
+    base += n;
     p.tile_off[n] = tiles;
     p.num_work = n;
     p.total_tiles = tiles;
@@ -483,11 +532,22 @@ int validate_decode(const hcp_decode_args* a) {
         a->block_table_stride <= 0 || a->block_table_rows <= 0 || !aligned16(a->kv_cache))
       return HCP_ERR_INVALID;
   }
+  if (a->num_ext < 0 || a->num_ext > HCP_MAX_EXT_SOURCES || (a->num_ext > 0 && a->ext == nullptr))
+    return HCP_ERR_INVALID;
+  for (int i = 0; i < a->num_ext; ++i) {
+    const hcp_kv_source& e = a->ext[i];
+    if (e.k == nullptr || e.v == nullptr || e.rows <= 0 || e.row_stride < kv_row || (e.row_stride % 8) != 0 ||
+        !aligned16(e.k) || !aligned16(e.v))
+      return HCP_ERR_INVALID;
+  }
   for (int i = 0; i < a->num_seqs; ++i) {
     const hcp_decode_seq& q = a->seqs[i];
     if (q.q_row < 0 || q.q_row >= a->q_rows || q.peer_len < 0 || q.local_len < 0 || q.peer_start < 0)
       return HCP_ERR_INVALID;
-    if (q.peer_len > 0 && (!peer || static_cast<int64_t>(q.peer_start) + q.peer_len > a->peer_rows))
+    const int src = a->peer_src != nullptr ? a->peer_src[i] : -1;
+    if (src < -1 || src >= a->num_ext) return HCP_ERR_INVALID;
+    const int64_t src_rows = src < 0 ? (peer ? a->peer_rows : 0) : a->ext[src].rows;
+    if (q.peer_len > 0 && static_cast<int64_t>(q.peer_start) + q.peer_len > src_rows)
       return HCP_ERR_INVALID;
     if (q.local_len > 0) {
       if (!paged || q.paged_req < 0 || q.paged_req >= a->block_table_rows || q.local_start < 0)
@@ -539,6 +599,16 @@ extern "C" int hcp_ring_decode_splitkv(const hcp_decode_args* a, void* stream) {
     const uint32_t box[4] = {64, static_cast<uint32_t>(bs), 1, 1};
     if (!encode_map(&p.tm_cache, f16, 4, a->kv_cache, dims, strides, box)) return HCP_ERR_CUDA;
   }
+  for (int i = 0; i < HCP_MAX_EXT_SOURCES; ++i) p.tm_epk[i] = p.tm_epv[i] = p.tm_pk;
+  for (int i = 0; i < a->num_ext; ++i) {
+    const hcp_kv_source& e = a->ext[i];
+    const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(Hkv), static_cast<uint64_t>(e.rows)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(D) * 2, static_cast<uint64_t>(e.row_stride) * 2};
+    const uint32_t box[3] = {64, 1, kDecTileKeys};
+    if (!encode_map(&p.tm_epk[i], f16, 3, e.k, dims, strides, box) ||
+        !encode_map(&p.tm_epv[i], f16, 3, e.v, dims, strides, box))
+      return HCP_ERR_CUDA;
+  }
   p.q = a->q;
   p.q_row_stride = a->q_row_stride;
   p.block_table = a->block_table;
@@ -561,7 +631,8 @@ extern "C" int hcp_ring_decode_splitkv(const hcp_decode_args* a, void* stream) {
     std::memset(&c, 0, sizeof(c));
     for (int i = 0; i < n; ++i) {
       const hcp_decode_seq& q = a->seqs[base + i];
-      p.seq[i] = DecodeSeq{q.q_row, q.peer_start, q.peer_len, q.paged_req, q.local_start, q.local_len};
+      p.seq[i] = DecodeSeq{q.q_row, q.peer_start, q.peer_len, q.paged_req, q.local_start, q.local_len,
+                           a->peer_src != nullptr ? a->peer_src[base + i] : -1};
       p.unit_off[i] = units;
       c.unit_off[i] = units;
       c.q_row[i] = q.q_row;

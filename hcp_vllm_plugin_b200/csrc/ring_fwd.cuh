@@ -131,6 +131,8 @@ struct FwdParams {
   FwdItem work[kMaxWork];
   hcp_kv_segment segs[kMaxSegs];
 };
+// Kernel arguments may take up to 32764 bytes (CUDA 12.1+, compute 7.0+).
+static_assert(sizeof(FwdParams) <= 32764, "forward kernel parameters too large");
 
 // Bounded mbarrier wait.  Returns false when this CTA aborted (this wait ran
 // out of time, another role of the CTA gave up, or another CTA failed).

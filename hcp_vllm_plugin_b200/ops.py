@@ -38,6 +38,25 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _ext_sources(ext, dtype):
+    """ctypes array of ``hcp_kv_source`` for a list of (k, v) tensors, each
+    [rows, Hkv, D] with its last two dims packed (k and v of one source share
+    a row stride), or None."""
+    if not ext:
+        return None
+    if len(ext) > C.HCP_MAX_EXT_SOURCES:
+        raise ValueError(f"at most {C.HCP_MAX_EXT_SOURCES} extra sources per call")
+    arr = (C.HcpKvSource * len(ext))()
+    for i, (k, v) in enumerate(ext):
+        if k.shape != v.shape or k.dtype != dtype or v.dtype != dtype or not k.is_cuda:
+            raise ValueError(f"extra source {i}: k and v must be CUDA tensors of one shape and q's dtype")
+        ks, vs = _rows_heads(k, f"ext[{i}].k"), _rows_heads(v, f"ext[{i}].v")
+        if ks != vs:
+            raise ValueError(f"extra source {i}: k and v must share a row stride")
+        arr[i].k, arr[i].v, arr[i].rows, arr[i].row_stride = _ptr(k), _ptr(v), k.shape[0], ks
+    return arr
+
+
 def make_work(items) -> np.ndarray:
     """Pack work items into an int32 [n, 12] array.
 
@@ -69,12 +88,17 @@ def ring_attn_fwd(
     block_table: torch.Tensor | None = None,
     merge_o: torch.Tensor | None = None,
     merge_lse: torch.Tensor | None = None,
+    ext=None,
+    seg_list: np.ndarray | None = None,
 ) -> None:
     """Fused ring-attention forward over a list of work items (``hcp_ring_attn_fwd``).
 
     q/out [rows, H, D]; k_*/v_* [rows, Hkv, D]; kv_cache [num_blocks, Hkv,
     block_size, 2*D]; block_table [num_reqs, max_blocks] int32; lse, merge_lse
-    [H, cols] float32.  ``work`` comes from :func:`make_work`.
+    [H, cols] float32.  ``work`` comes from :func:`make_work`.  ``ext``: up to
+    8 extra contiguous (k, v) sources, named by segments as
+    ``HCP_SRC_EXT0 + i``; ``seg_list``: int32 [n, 4] segments that
+    ``HCP_SRC_LIST`` items point into (``(HCP_SRC_LIST, first, count, 0)``).
     """
     if not q.is_cuda:
         raise ValueError("q must be a CUDA tensor (no CPU path)")
@@ -137,6 +161,13 @@ def ring_attn_fwd(
         a.merge_o_row_stride = _rows_heads(merge_o, "merge_o")
         a.merge_lse = _ptr(merge_lse)
         a.merge_lse_stride = merge_lse.stride(0)
+    ext_arr = _ext_sources(ext, q.dtype)
+    if ext_arr is not None:
+        a.ext, a.num_ext = ctypes.cast(ext_arr, ctypes.POINTER(C.HcpKvSource)), len(ext_arr)
+    if seg_list is not None:
+        seg_list = np.ascontiguousarray(seg_list, dtype=np.int32).reshape(-1, 4)
+        a.seg_list = seg_list.ctypes.data_as(ctypes.POINTER(C.HcpKvSegment))
+        a.num_seg_list = seg_list.shape[0]
     work = np.ascontiguousarray(work, dtype=np.int32)
     a.work = work.ctypes.data_as(ctypes.POINTER(C.HcpAttnWork))
     a.num_work = work.shape[0]
@@ -234,8 +265,11 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
 
 
 def decode_args(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, peer_v=None,
-                kv_cache=None, block_table=None, chunk_keys=0):
-    """Build ``hcp_decode_args`` (without workspace) plus the packed sequence array."""
+                kv_cache=None, block_table=None, chunk_keys=0, ext=None, peer_src=None):
+    """Build ``hcp_decode_args`` (without workspace) plus the host arrays it
+    points to (keep them alive until the call).  ``ext``: extra contiguous
+    (k, v) peer sources; ``peer_src``: per sequence, -1 for peer_k / peer_v or
+    the index of its extra source."""
     if not q.is_cuda or q.dtype not in (torch.bfloat16, torch.float16):
         raise ValueError("q must be a bf16/fp16 CUDA tensor (no CPU path)")
     seqs = np.ascontiguousarray(seqs, dtype=np.int32).reshape(-1, DECODE_FIELDS)
@@ -268,11 +302,20 @@ def decode_args(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, pee
         a.lse, a.lse_stride = _ptr(lse), lse.stride(0)
     a.seqs = seqs.ctypes.data_as(ctypes.POINTER(C.HcpDecodeSeq))
     a.num_seqs = seqs.shape[0]
-    return a, seqs
+    ext_arr = _ext_sources(ext, q.dtype)
+    if ext_arr is not None:
+        a.ext, a.num_ext = ctypes.cast(ext_arr, ctypes.POINTER(C.HcpKvSource)), len(ext_arr)
+    if peer_src is not None:
+        peer_src = np.ascontiguousarray(peer_src, dtype=np.int32).reshape(-1)
+        if peer_src.shape[0] != seqs.shape[0]:
+            raise ValueError("peer_src needs one entry per sequence")
+        a.peer_src = peer_src.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))
+    return a, (seqs, ext_arr, peer_src)
 
 
 def decode_splitkv(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, peer_v=None,
-                   kv_cache=None, block_table=None, chunk_keys=0, workspace=None):
+                   kv_cache=None, block_table=None, chunk_keys=0, workspace=None, ext=None,
+                   peer_src=None):
     """Batch-merged split-KV decode (``hcp_ring_decode_splitkv``).
 
     ``seqs`` rows: (q_row, peer_start, peer_len, paged_req, local_start,
@@ -280,7 +323,7 @@ def decode_splitkv(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, 
     """
     a, keep = decode_args(q, seqs, scale=scale, num_kv_heads=num_kv_heads, out=out, lse=lse,
                           peer_k=peer_k, peer_v=peer_v, kv_cache=kv_cache,
-                          block_table=block_table, chunk_keys=chunk_keys)
+                          block_table=block_table, chunk_keys=chunk_keys, ext=ext, peer_src=peer_src)
     lib = C.load()
     need = lib.hcp_decode_workspace_bytes(ctypes.byref(a))
     if need < 0:

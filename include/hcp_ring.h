@@ -189,6 +189,12 @@ typedef struct hcp_decode_args {
   const hcp_decode_seq* seqs;  /* HOST array */
   int32_t num_seqs;
   int32_t _pad2;
+  /* Optional: extra contiguous peer sources (HOST array, <= HCP_MAX_EXT_SOURCES)
+   * and, per sequence, where its peer keys are (HOST array of num_seqs:
+   * -1 = peer_k / peer_v, i = ext[i]); NULL / 0 = every sequence uses
+   * peer_k / peer_v.  Each request's staged chunk is read as it lies. */
+  const hcp_kv_source* ext;   int32_t num_ext;   int32_t _pad3;
+  const int32_t* peer_src;
 } hcp_decode_args;
 
 /*
