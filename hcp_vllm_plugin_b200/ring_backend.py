@@ -37,7 +37,7 @@ from vllm.v1.attention.backends.flash_attn import (
 )
 
 from . import ops
-from .ring_plan import misaligned_paged_starts, plan_layer
+from .ring_plan import CONCAT, misaligned_paged_starts, plan_layer
 
 logger = init_logger(__name__)
 _LAYER_RE = re.compile(r"layers\.(\d+)\.")
@@ -368,28 +368,29 @@ class HcpRingAttentionImpl(AttentionImpl):
             if misaligned_paged_starts(plan, block_size):
                 raise ValueError("HCP ring backend: peer prefix length must be a multiple of the block size")
             plans[sig] = plan
-        parts = [kv for r in plan.part_requests for kv in peers[r]]
-        k_a = v_a = None
-        if parts:
-            if len(parts) == 1:
-                k_a, v_a = parts[0]
-            else:
-                # several staged chunks (or requests): one peer arena per layer
-                k_a = torch.cat([k for k, _ in parts], dim=0)
-                v_a = torch.cat([v for _, v in parts], dim=0)
-                IMPL_STATS["peer_concat"] += 1
         block_table = attn_metadata.block_table
         if block_table.dtype != torch.int32:
             block_table = block_table.to(torch.int32)
-        if plan.work.shape[0]:
-            ops.ring_attn_fwd(q, plan.work, scale=self.scale, num_kv_heads=self.num_kv_heads, out=out,
-                              k_a=k_a, v_a=v_a, kv_cache=kv_cache, block_table=block_table)
-            IMPL_STATS["attn_cuda"] += 1
-        if plan.decode.shape[0]:
-            ops.decode_splitkv(q, plan.decode, scale=self.scale, num_kv_heads=self.num_kv_heads,
-                               out=out, peer_k=k_a, peer_v=v_a, kv_cache=kv_cache,
-                               block_table=block_table)
-            IMPL_STATS["decode_cuda"] += 1
+        for grp in plan.groups:
+            # each staged chunk is read where it lies (an extra source of the
+            # kernels); only a request with more chunks than a work item has
+            # segments for is concatenated
+            ext = []
+            for r, c in grp.sources:
+                if c == CONCAT:
+                    ext.append((torch.cat([k for k, _ in peers[r]], dim=0),
+                                torch.cat([v for _, v in peers[r]], dim=0)))
+                    IMPL_STATS["peer_concat"] += 1
+                else:
+                    ext.append(peers[r][c])
+            if grp.work.shape[0]:
+                ops.ring_attn_fwd(q, grp.work, scale=self.scale, num_kv_heads=self.num_kv_heads, out=out,
+                                  kv_cache=kv_cache, block_table=block_table, ext=ext, seg_list=grp.seg_list)
+                IMPL_STATS["attn_cuda"] += 1
+            if grp.decode.shape[0]:
+                ops.decode_splitkv(q, grp.decode, scale=self.scale, num_kv_heads=self.num_kv_heads, out=out,
+                                   kv_cache=kv_cache, block_table=block_table, ext=ext, peer_src=grp.peer_src)
+                IMPL_STATS["decode_cuda"] += 1
         if ring_rows:
             self._decode_ring_forward(layer_index(layer_name), ring_rows, qsl, seq_lens, q, key, value,
                                       kv_cache, block_table, out)
