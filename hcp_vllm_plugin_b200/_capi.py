@@ -155,6 +155,7 @@ SIGNATURES = {
         ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     "hcp_get_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "hcp_reset_device_status": (ctypes.c_int, []),
+    "hcp_device_status_async": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "hcp_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_int64, ctypes.POINTER(ctypes.c_int32)]),
     "hcp_version": (ctypes.c_char_p, []),
 }
@@ -199,3 +200,35 @@ def device_status() -> int:
 
 def reset_device_status() -> None:
     check(load().hcp_reset_device_status(), "hcp_reset_device_status")
+
+
+class DeviceStatusWatch:
+    """The library's device status word, watched without synchronising:
+    :meth:`record` queues a copy of it into a pinned host word behind the
+    work already on a stream; :meth:`check` raises :class:`HcpError` when a
+    copy that has completed saw a failure (a bounded wait that ran out, after
+    which every later kernel of the library skips its work)."""
+
+    def __init__(self):
+        import torch
+
+        self._torch = torch
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+
+    def record(self, stream) -> None:
+        torch = self._torch
+        check(load().hcp_device_status_async(self.host.data_ptr(), stream.cuda_stream),
+              "hcp_device_status_async")
+        self.event = torch.cuda.Event()
+        self.event.record(stream)
+
+    def check(self, what: str = "device") -> None:
+        if self.event is None or not self.event.query():
+            return
+        v = int(self.host[0])
+        if v != 0:
+            self.event = None
+            raise HcpError(f"{what}: a kernel of this library reported a device-side failure {v:#x} "
+                           f"(a bounded wait ran out); later kernels skip their work until "
+                           f"hcp_reset_device_status")

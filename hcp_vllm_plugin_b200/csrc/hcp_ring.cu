@@ -485,6 +485,14 @@ extern "C" int hcp_get_device_status(int32_t* status_out) {
   return HCP_OK;
 }
 
+extern "C" int hcp_device_status_async(int32_t* host_out, void* stream) {
+  if (host_out == nullptr) return HCP_ERR_INVALID;
+  return cudaMemcpyFromSymbolAsync(host_out, g_device_status, sizeof(int), 0, cudaMemcpyDeviceToHost,
+                                   static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? HCP_OK
+             : HCP_ERR_CUDA;
+}
+
 extern "C" int hcp_reset_device_status(void) {
   const int zero = 0;
   if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return HCP_ERR_CUDA;

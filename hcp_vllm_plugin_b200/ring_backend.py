@@ -36,7 +36,7 @@ from vllm.v1.attention.backends.flash_attn import (
     FlashAttentionMetadataBuilder,
 )
 
-from . import ops
+from . import _capi, ops
 from .ring_plan import CONCAT, misaligned_paged_starts, plan_layer
 
 logger = init_logger(__name__)
@@ -63,6 +63,16 @@ BATCH_STATS: dict = {"max_reqs": 0}
 # Which device paths ran (validation evidence, as the reference's IMPL_STATS).
 IMPL_STATS: dict = {"attn_cuda": 0, "decode_cuda": 0, "cache_update_cuda": 0, "peer_concat": 0,
                     "decode_ring": 0}
+
+
+_STATUS_WATCH: dict = {}  # device index -> _capi.DeviceStatusWatch
+
+
+def _status_watch(device: torch.device):
+    w = _STATUS_WATCH.get(device.index)
+    if w is None:
+        w = _STATUS_WATCH[device.index] = _capi.DeviceStatusWatch()
+    return w
 
 
 def stage_peer_kv(chunk_key: str, layer_name: str, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -293,6 +303,10 @@ class HcpRingAttentionImpl(AttentionImpl):
         qsl = attn_metadata.query_start_loc.tolist()
         seq_lens = attn_metadata.seq_lens.tolist()
         bt0 = attn_metadata.block_table[: len(seq_lens), 0].tolist()
+        if attn_metadata.query_start_loc.is_cuda:
+            # the step's one synchronisation has just passed: a device-side
+            # failure of an earlier step surfaces here as an HcpError
+            _status_watch(attn_metadata.query_start_loc.device).check("HCP ring backend")
         cached = (qsl, seq_lens, bt0)
         try:
             attn_metadata._hcp_host_meta = cached
@@ -394,6 +408,8 @@ class HcpRingAttentionImpl(AttentionImpl):
         if ring_rows:
             self._decode_ring_forward(layer_index(layer_name), ring_rows, qsl, seq_lens, q, key, value,
                                       kv_cache, block_table, out)
+        if q.is_cuda:
+            _status_watch(q.device).record(torch.cuda.current_stream(q.device))
         return output
 
     # -- memory-split decode -------------------------------------------------

@@ -47,7 +47,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _capi, ops
 
 OP_STOP, OP_STEP = 0, 1
 _HDR = "hcp_decode_ring/hdr/"
@@ -217,6 +217,8 @@ class RingDecode:
         self._seq = 0                      # control-plane header sequence
         self.steps_served = 0
         self.launches = 0  # kernels of this library launched (for counting in benchmarks)
+        # device-side failures of earlier steps surface as HcpError at the next step
+        self._watch = _capi.DeviceStatusWatch() if device.type == "cuda" else None
 
     # ------------------------------------------------------------------ setup
     def install_rows(self, layer: int, slot: int, n: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -252,6 +254,8 @@ class RingDecode:
         slots = list(range(n)) if slots is None else [int(s) for s in slots]
         if n == 0:
             return out
+        if self._watch is not None:
+            self._watch.check("decode ring")
         if n > self.B or len(slots) != n:
             raise ValueError(f"a step of {n} requests (slots {slots}) for {self.B} slots")
         H, D, Hkv = self.H, self.D, self.Hkv
@@ -266,16 +270,21 @@ class RingDecode:
         kb = pay[nq:nq + nk].view(n, Hkv, D)
         vb = pay[nq + nk:].view(n, Hkv, D)
         lens = self.lens[layer]
-        mine, rows = [], []
-        for i, (s, pos) in enumerate(zip(slots, positions)):
-            if growth_assignee(int(pos), self.world, self.policy) != self.rank:
-                continue
-            if lens[s] >= self.cap:
+        mine = [i for i, pos in enumerate(positions)
+                if growth_assignee(int(pos), self.world, self.policy) == self.rank]
+        # every token this rank keeps must fit before any state changes
+        extra: dict[int, int] = {}
+        for i in mine:
+            extra[slots[i]] = extra.get(slots[i], 0) + 1
+        for s, e in extra.items():
+            if lens[s] + e > self.cap:
                 raise RuntimeError(f"slot {s}: growth exceeds the capacity {self.cap} on rank {self.rank}")
-            mine.append(i)
+        rows = []
+        for i in mine:
+            s = slots[i]
             rows.append(s * self.cap + lens[s])
             lens[s] += 1
-            self.growth_positions[layer][s].append(int(pos))
+            self.growth_positions[layer][s].append(int(positions[i]))
         if mine:
             # every token this rank keeps, in one copy for K and one for V
             src = torch.tensor(mine, dtype=torch.long).to(self.device, non_blocking=True)
@@ -291,6 +300,8 @@ class RingDecode:
         self.launches += 1
         parts = [p[:nq + H * n] for p in self._parts] if self.rank == self.owner else None
         self.comm.gather(part, self.owner, parts)
+        if self._watch is not None:
+            self._watch.record(torch.cuda.current_stream(self.device))
         if self.rank != self.owner:
             return None
         states_o = torch.stack([p[:nq].view(n, H, D) for p in parts])

@@ -117,6 +117,8 @@ class RingPrefill:
             self.s_hop = torch.cuda.Stream(device, priority=-100)   # clamped to the highest
             self.s_comm = torch.cuda.Stream(device, priority=-100)
             self.slot_free = [torch.cuda.Event() for _ in self.slot_k]
+        # device-side failures of earlier layers surface as HcpError at the next
+        self._watch = C.DeviceStatusWatch() if self._cuda else None
         if self.world > 1:
             # NCCL wants every rank of a group in its first collective; the
             # per-hop send/recv calls involve only pairs
@@ -161,8 +163,12 @@ class RingPrefill:
         stream."""
         x, c = self.rank, self.chunk
         A, B = C.HCP_SRC_A, C.HCP_SRC_B
+        if self._watch is not None:
+            self._watch.check("ring prefill")
         if self.world == 1:
             self._attn(q, [(0, c, 0, 0, (A, 0, c, 0), None)], out, lse, k_a=k, v_a=v)
+            if self._watch is not None:
+                self._watch.record(torch.cuda.current_stream(self.device))
             return out
         if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
             raise ValueError("ring prefill: q, k and v must be contiguous (they are sent as they are)")
@@ -276,4 +282,6 @@ class RingPrefill:
         # the caller may overwrite q/k/v once this returns: wait for the sends
         for w in send_works:
             w.wait()
+        if self._watch is not None:
+            self._watch.record(s0)
         return out

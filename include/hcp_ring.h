@@ -329,6 +329,16 @@ int hcp_get_device_status(int32_t* status_out);
 int hcp_reset_device_status(void);
 
 /*
+ * Stream-ordered copy of the device status word into host memory (use pinned
+ * memory for a copy that does not block): the value is valid once the work
+ * queued on `stream` before this call has finished.  Lets a serving loop
+ * notice a device-side failure at its next synchronisation without adding
+ * one.  No counterpart in the reference (its launch errors raise in Python,
+ * hcp_vllm_plugin/ring_backend.py:333-336).
+ */
+int hcp_device_status_async(int32_t* host_out, void* stream);
+
+/*
  * Failure-path self-test: launches one thread that waits, through the
  * kernels' own bounded mbarrier wait, on a barrier nothing arrives on, for
  * timeout_ns (at most 2 s).  The wait runs out, the device status becomes

@@ -67,6 +67,7 @@ def test_backend_forward_matches_reference_forward():
     rb.clear_peer_kv()
     assert len(meta._hcp_plans) == 1 and torch.equal(out, out2)
     assert rb.IMPL_STATS["attn_cuda"] == 2 and rb.IMPL_STATS["decode_cuda"] == 2
+    assert rb.IMPL_STATS["peer_concat"] == 0  # the 3-chunk prefix is read where it is staged
     got = out[:ntok].float().cpu().numpy()
     ref_out = ro.bf16_bits_to_f32(z["output"])  # the reference forward's own (bf16) output
     # the fp32 values behind it: the oracle's restatement of the same forward

@@ -71,6 +71,40 @@ def test_cfg2_full_size(dev):
     print(st.line())
 
 
+def test_decode_peer_keys_in_separate_sources(dev):
+    """Each sequence's peer keys in its own staged tensor (an extra source,
+    peer_src), or the common peer arena, or none: equal to the oracle."""
+    from hcp_vllm_plugin_b200 import ops
+    q, pk, pv, cache, bt, seqs = _decode_case([700, 0, 300, 1000], [500, 129, 0, 2048], seed=5)
+    g = torch.Generator(device="cpu").manual_seed(6)
+    own = {0: 700, 3: 1000}  # sequences 0 and 3 read their own tensors
+    ext, src = [], []
+    for r in range(4):
+        if r in own:
+            k = torch.randn(own[r] + 16, 4, 128, generator=g).bfloat16()
+            v = torch.randn(own[r] + 16, 4, 128, generator=g).bfloat16()
+            ext.append((k, v))
+            seqs[r][1] = 16          # start inside the source
+            src.append(len(ext) - 1)
+        else:
+            src.append(-1)
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=dev)
+    ops.decode_splitkv(q.to(dev), seqs, scale=128 ** -0.5, num_kv_heads=4, out=out, lse=lse,
+                       peer_k=pk.to(dev), peer_v=pv.to(dev), kv_cache=cache.to(dev),
+                       block_table=torch.from_numpy(bt).to(dev), chunk_keys=256,
+                       ext=[(k.to(dev), v.to(dev)) for k, v in ext], peer_src=np.array(src, np.int32))
+    torch.cuda.synchronize()
+    for r, (qr, ps, pl, preq, ls, ll) in enumerate(seqs):
+        kp_, vp_ = (ext[src[r]] if src[r] >= 0 else (pk, pv))
+        kloc, vloc = ro.paged_gather(_f(cache), bt[preq], ls + ll)
+        k = np.concatenate([_f(kp_[ps:ps + pl]), kloc[ls:]], 0)
+        v = np.concatenate([_f(vp_[ps:ps + pl]), vloc[ls:]], 0)
+        want, want_lse = ro.attn_with_lse(_f(q[qr:qr + 1]), k, v, 128 ** -0.5, None)
+        P.check_out(_f(out[qr]), want[0], f"decode source {src[r]} seq {r}")
+        P.check_lse(_f(lse[:, qr]), want_lse[:, 0], f"decode source {src[r]} seq {r}")
+
+
 def test_decode_fp16_d64(dev):
     from hcp_vllm_plugin_b200 import ops
     q, pk, pv, cache, bt, seqs = _decode_case([512, 100], [700, 33], h=14, hkv=2, d=64,

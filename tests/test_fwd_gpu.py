@@ -226,3 +226,50 @@ def test_paged_local_plus_peer_batch(dev, lens, peer):
     if peer >= 512:
         P.check_flat(_f(out), want, f"paged batch {lens} (cfg1 shape)")
     print(st.line())
+
+
+def test_segment_lists_over_separate_chunks(dev):
+    """Work items whose peer keys sit in several separately allocated chunks
+    (extra sources, as staged) plus paged local keys, as segment lists of up
+    to 8 segments, equal the oracle over the concatenated keys; an inline
+    item reading an extra source rides in the same launch."""
+    from hcp_vllm_plugin_b200 import _capi as C, ops
+    g = torch.Generator(device="cpu").manual_seed(77)
+    E = C.HCP_SRC_EXT0
+    b = P.paged_batch([300, 129, 1], 0, seed=7)  # paged local keys only; peers come from chunks
+    chunk_lens = [[256, 128, 512], [64] * 7, [1000]]
+    chunks = [[(torch.randn(n, HKV4, D128, generator=g).bfloat16(), torch.randn(n, HKV4, D128, generator=g).bfloat16())
+               for n in lens] for lens in chunk_lens]
+    ext, seg_list, items = [], [], []
+    for r, L in enumerate(b["lens"]):
+        segs = []
+        for k, v in chunks[r]:
+            segs.append((E + len(ext), 0, k.shape[0], -1))
+            ext.append((k.to(dev), v.to(dev)))
+        segs.append((C.HCP_SRC_PAGED, 0, L, 0))
+        qs = int(b["qsl"][r])
+        if len(segs) <= 2:
+            items.append((qs, L, r, qs, segs[0], segs[1]))
+        else:
+            items.append((qs, L, r, qs, (C.HCP_SRC_LIST, len(seg_list), len(segs), 0), None))
+            seg_list.extend(segs)
+    assert len(ext) == 11
+    # more than 8 sources: two calls, split by request
+    q = b["q"].to(dev)
+    out = torch.empty_like(q)
+    lse = torch.empty(H28, q.shape[0], dtype=torch.float32, device=dev)
+    cache, bt = b["cache"].to(dev), torch.from_numpy(b["bt"]).to(dev)
+    kw = dict(scale=D128 ** -0.5, num_kv_heads=HKV4, out=out, lse=lse, kv_cache=cache, block_table=bt)
+    ops.ring_attn_fwd(q, ops.make_work(items[:1]), ext=ext[:3], seg_list=np.array(seg_list[:4]), **kw)
+    sl2 = [(s[0] - 3 if s[0] >= E else s[0], *s[1:]) for s in seg_list[4:]]
+    it2 = [items[1][:4] + ((C.HCP_SRC_LIST, 0, 8, 0), None), items[2][:4] + ((E + 7, 0, 1000, -1),) + items[2][5:]]
+    ops.ring_attn_fwd(q, ops.make_work(it2), ext=ext[3:], seg_list=np.array(sl2), **kw)
+    torch.cuda.synchronize()
+    for r, L in enumerate(b["lens"]):
+        qs = int(b["qsl"][r])
+        kl, vl = ro.paged_gather(_f(b["cache"]), b["bt"][r], L)
+        k = np.concatenate([_f(c[0]) for c in chunks[r]] + [kl], 0)
+        v = np.concatenate([_f(c[1]) for c in chunks[r]] + [vl], 0)
+        want, want_lse = ro.attn_with_lse(_f(b["q"][qs:qs + L]), k, v, D128 ** -0.5, sum(chunk_lens[r]))
+        P.check_out(_f(out[qs:qs + L]), want, f"segment list request {r}")
+        P.check_lse(_f(lse[:, qs:qs + L]), want_lse, f"segment list request {r}")
