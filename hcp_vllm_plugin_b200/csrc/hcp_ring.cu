@@ -47,6 +47,21 @@ EncodeTiledFn encode_fn() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Kernels launch on the current device.  A stream that belongs to another
+// device is refused (HCP_ERR_INVALID) instead of receiving kernels whose
+// addresses and tensor maps were made for that other device.  0, 1 and 2 are
+// the runtime's default / legacy / per-thread streams of the current device.
+bool stream_on_current_device(void* stream) {
+  if (reinterpret_cast<uintptr_t>(stream) <= 2) return true;
+  int cur = -1, sdev = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess) return false;
+  if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return cur == sdev;
+}
+
 // log2(n) when n is a power of two, else -1
 int pow2_shift(int n) {
   if (n <= 0 || (n & (n - 1)) != 0) return -1;
@@ -223,6 +238,7 @@ int64_t workspace_need(const hcp_decode_args* a, int chunk) {
 using namespace hcp;
 
 extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
+  if (!stream_on_current_device(stream)) return HCP_ERR_INVALID;
   if (a == nullptr) return HCP_ERR_INVALID;
   if (a->dtype != HCP_BF16 && a->dtype != HCP_F16) return HCP_ERR_UNSUPPORTED;
   const bool f16 = a->dtype == HCP_F16;
@@ -404,6 +420,7 @@ extern "C" int hcp_merge_attn_states(void* out, int32_t out_dtype, int64_t out_r
                                      int64_t suffix_row_stride, const float* suffix_lse,
                                      int64_t suffix_lse_stride, int64_t num_tokens,
                                      int32_t num_heads, int32_t head_dim, void* stream) {
+  if (!stream_on_current_device(stream)) return HCP_ERR_INVALID;
   auto ok_dt = [](int dt) { return dt == HCP_BF16 || dt == HCP_F16 || dt == HCP_F32; };
   if (out == nullptr || prefix_o == nullptr || suffix_o == nullptr || prefix_lse == nullptr ||
       suffix_lse == nullptr)
@@ -447,6 +464,7 @@ extern "C" int hcp_merge_attn_states_n(void* out, int32_t out_dtype, int64_t out
                                        float* out_lse, int64_t out_lse_stride, const float* states_o,
                                        const float* states_lse, int32_t num_states, int64_t num_tokens,
                                        int32_t num_heads, int32_t head_dim, void* stream) {
+  if (!stream_on_current_device(stream)) return HCP_ERR_INVALID;
   if (out == nullptr || states_o == nullptr || states_lse == nullptr) return HCP_ERR_INVALID;
   if (out_dtype != HCP_BF16 && out_dtype != HCP_F16 && out_dtype != HCP_F32) return HCP_ERR_UNSUPPORTED;
   if (num_states <= 0 || num_tokens < 0 || num_heads <= 0 || head_dim <= 0) return HCP_ERR_INVALID;
@@ -486,6 +504,7 @@ extern "C" int hcp_get_device_status(int32_t* status_out) {
 }
 
 extern "C" int hcp_device_status_async(int32_t* host_out, void* stream) {
+  if (!stream_on_current_device(stream)) return HCP_ERR_INVALID;
   if (host_out == nullptr) return HCP_ERR_INVALID;
   return cudaMemcpyFromSymbolAsync(host_out, g_device_status, sizeof(int), 0, cudaMemcpyDeviceToHost,
                                    static_cast<cudaStream_t>(stream)) == cudaSuccess
@@ -576,6 +595,7 @@ extern "C" int64_t hcp_decode_workspace_bytes(const hcp_decode_args* a) {
 }
 
 extern "C" int hcp_ring_decode_splitkv(const hcp_decode_args* a, void* stream) {
+  if (!stream_on_current_device(stream)) return HCP_ERR_INVALID;
   const int rc0 = validate_decode(a);
   if (rc0 != HCP_OK) return rc0;
   if (a->num_seqs == 0) return HCP_OK;
@@ -678,6 +698,7 @@ extern "C" int hcp_kv_cache_update(const void* key, const void* value, int64_t n
                                    const int64_t* slot_mapping, void* kv_cache, int64_t num_blocks,
                                    int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
                                    int32_t dtype, void* stream) {
+  if (!stream_on_current_device(stream)) return HCP_ERR_INVALID;
   if (dtype != HCP_BF16 && dtype != HCP_F16) return HCP_ERR_UNSUPPORTED;
   if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || (head_dim % 8) != 0 || block_size <= 0 ||
       num_blocks <= 0)
@@ -712,6 +733,7 @@ extern "C" int hcp_kv_cache_gather(const void* kv_cache, int64_t num_blocks, int
                                    int32_t num_kv_heads, int32_t head_dim, const int64_t* slot_mapping,
                                    int64_t num_tokens, void* key, void* value, int64_t key_row_stride,
                                    int64_t value_row_stride, int32_t dtype, void* stream) {
+  if (!stream_on_current_device(stream)) return HCP_ERR_INVALID;
   if (dtype != HCP_BF16 && dtype != HCP_F16) return HCP_ERR_UNSUPPORTED;
   if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || (head_dim % 8) != 0 || block_size <= 0 ||
       num_blocks <= 0)

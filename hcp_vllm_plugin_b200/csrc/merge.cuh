@@ -37,6 +37,8 @@ __device__ __forceinline__ void store_elem(void* base, int dt, long long i, floa
 }
 
 __global__ void __launch_bounds__(256) merge_states_kernel(const MergeParams p) {
+  // after a recorded failure the partials may be unwritten: leave out alone
+  if (*reinterpret_cast<volatile int*>(&g_device_status) != 0) return;
   const long long warp_global = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const long long rows = p.num_tokens * p.num_heads;
@@ -88,6 +90,7 @@ struct MergeNParams {
 };
 
 __global__ void __launch_bounds__(256) merge_states_n_kernel(const MergeNParams p) {
+  if (*reinterpret_cast<volatile int*>(&g_device_status) != 0) return;
   const long long warp_global = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const long long rows = p.num_tokens * p.num_heads;

@@ -38,6 +38,12 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _dev(t: torch.Tensor):
+    """Make the tensor's GPU the current device for the library call: the
+    library launches on the current device, into a stream of that device."""
+    return torch.cuda.device(t.device)
+
+
 def _ext_sources(ext, dtype):
     """ctypes array of ``hcp_kv_source`` for a list of (k, v) tensors, each
     [rows, Hkv, D] with its last two dims packed (k and v of one source share
@@ -171,7 +177,8 @@ def ring_attn_fwd(
     work = np.ascontiguousarray(work, dtype=np.int32)
     a.work = work.ctypes.data_as(ctypes.POINTER(C.HcpAttnWork))
     a.num_work = work.shape[0]
-    C.check(C.load().hcp_ring_attn_fwd(ctypes.byref(a), _stream(q)), "hcp_ring_attn_fwd")
+    with _dev(q):
+        C.check(C.load().hcp_ring_attn_fwd(ctypes.byref(a), _stream(q)), "hcp_ring_attn_fwd")
 
 
 def ring_attn_with_lse(
@@ -217,14 +224,15 @@ def merge_attn_states(
         if t.dtype != torch.float32 or t.stride(1) != 1:
             raise ValueError("lse tensors must be float32 with unit column stride")
     lib = C.load()
-    rc = lib.hcp_merge_attn_states(
-        _ptr(output), _DT[output.dtype], _rows_heads(output, "output"),
-        _ptr(output_lse), 0 if output_lse is None else output_lse.stride(0),
-        _ptr(prefix_output), _DT[prefix_output.dtype], _rows_heads(prefix_output, "prefix_output"),
-        _ptr(prefix_lse), prefix_lse.stride(0),
-        _ptr(suffix_output), _DT[suffix_output.dtype], _rows_heads(suffix_output, "suffix_output"),
-        _ptr(suffix_lse), suffix_lse.stride(0),
-        num_tokens, num_heads, head_dim, _stream(output))
+    with _dev(output):
+        rc = lib.hcp_merge_attn_states(
+            _ptr(output), _DT[output.dtype], _rows_heads(output, "output"),
+            _ptr(output_lse), 0 if output_lse is None else output_lse.stride(0),
+            _ptr(prefix_output), _DT[prefix_output.dtype], _rows_heads(prefix_output, "prefix_output"),
+            _ptr(prefix_lse), prefix_lse.stride(0),
+            _ptr(suffix_output), _DT[suffix_output.dtype], _rows_heads(suffix_output, "suffix_output"),
+            _ptr(suffix_lse), suffix_lse.stride(0),
+            num_tokens, num_heads, head_dim, _stream(output))
     C.check(rc, "hcp_merge_attn_states")
 
 
@@ -242,10 +250,11 @@ def merge_attn_states_n(output: torch.Tensor, states_o: torch.Tensor, states_lse
         raise ValueError("output must be [T, H, D]")
     if output_lse is not None and (output_lse.dtype != torch.float32 or output_lse.stride(1) != 1):
         raise ValueError("output_lse must be float32 with unit column stride")
-    rc = C.load().hcp_merge_attn_states_n(
-        _ptr(output), _DT[output.dtype], _rows_heads(output, "output"), _ptr(output_lse),
-        0 if output_lse is None else output_lse.stride(0), _ptr(states_o), _ptr(states_lse), n, t, h, d,
-        _stream(output))
+    with _dev(output):
+        rc = C.load().hcp_merge_attn_states_n(
+            _ptr(output), _DT[output.dtype], _rows_heads(output, "output"), _ptr(output_lse),
+            0 if output_lse is None else output_lse.stride(0), _ptr(states_o), _ptr(states_lse), n, t, h, d,
+            _stream(output))
     C.check(rc, "hcp_merge_attn_states_n")
 
 
@@ -330,7 +339,8 @@ def decode_splitkv(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, 
         raise C.HcpError("hcp_decode_workspace_bytes: invalid arguments")
     ws = workspace if workspace is not None else _workspace(q.device, need)
     a.workspace, a.workspace_bytes = _ptr(ws), ws.numel() * ws.element_size()
-    C.check(lib.hcp_ring_decode_splitkv(ctypes.byref(a), _stream(q)), "hcp_ring_decode_splitkv")
+    with _dev(q):
+        C.check(lib.hcp_ring_decode_splitkv(ctypes.byref(a), _stream(q)), "hcp_ring_decode_splitkv")
     del keep
 
 
@@ -355,9 +365,10 @@ def kv_cache_gather(kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
         value = torch.empty(n, hkv, d2 // 2, dtype=kv_cache.dtype, device=kv_cache.device)
     if key.shape[0] < n or value.shape[0] < n or key.dtype != kv_cache.dtype or value.dtype != kv_cache.dtype:
         raise ValueError("key/value must hold n rows of the cache's dtype")
-    rc = C.load().hcp_kv_cache_gather(
-        _ptr(kv_cache), nb, bs, hkv, d2 // 2, _ptr(slot_mapping), n, _ptr(key), _ptr(value),
-        _rows_heads(key, "key"), _rows_heads(value, "value"), _DT[kv_cache.dtype], _stream(kv_cache))
+    with _dev(kv_cache):
+        rc = C.load().hcp_kv_cache_gather(
+            _ptr(kv_cache), nb, bs, hkv, d2 // 2, _ptr(slot_mapping), n, _ptr(key), _ptr(value),
+            _rows_heads(key, "key"), _rows_heads(value, "value"), _DT[kv_cache.dtype], _stream(kv_cache))
     C.check(rc, "hcp_kv_cache_gather")
     return key, value
 
@@ -374,8 +385,9 @@ def kv_cache_update(key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tens
     if kv_cache.dim() != 4 or not kv_cache.is_contiguous() or kv_cache.dtype != key.dtype:
         raise ValueError("kv_cache must be a contiguous [num_blocks, Hkv, block_size, 2*D] tensor")
     n = min(slot_mapping.shape[0], key.shape[0])
-    rc = C.load().hcp_kv_cache_update(
-        _ptr(key), _ptr(value), n, _rows_heads(key, "key"), _rows_heads(value, "value"),
-        _ptr(slot_mapping), _ptr(kv_cache), kv_cache.shape[0], kv_cache.shape[2], key.shape[1],
-        key.shape[2], _DT[key.dtype], _stream(key))
+    with _dev(key):
+        rc = C.load().hcp_kv_cache_update(
+            _ptr(key), _ptr(value), n, _rows_heads(key, "key"), _rows_heads(value, "value"),
+            _ptr(slot_mapping), _ptr(kv_cache), kv_cache.shape[0], kv_cache.shape[2], key.shape[1],
+            key.shape[2], _DT[key.dtype], _stream(key))
     C.check(rc, "hcp_kv_cache_update")

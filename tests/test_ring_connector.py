@@ -411,8 +411,8 @@ def _cross_process(tmp_path, prod_dev: int, cons_dev: int):
             assert proc.poll() is None, "producer exited early"
             assert time.time() - t0 < 300, "producer did not publish its chunk"
             time.sleep(0.05)
-        torch.cuda.set_device(cons_dev)
-        _consume_and_check(shared, f"cuda:{cons_dev}", seed=12)
+        with torch.cuda.device(cons_dev):   # restores the current device afterwards
+            _consume_and_check(shared, f"cuda:{cons_dev}", seed=12)
     finally:
         open(os.path.join(shared, "done"), "w").close()
         assert proc.wait(timeout=240) == 0
