@@ -103,19 +103,23 @@ bool encode_rows_heads(CUtensorMap* m, bool f16, const void* base, int64_t rows,
 }
 
 std::mutex g_attr_mu;
-bool g_attr_done[2][2][3][64];
+bool g_attr_done[2][2][6][64];
 bool g_dec_attr_done[2][2][64];
 
-// Forward kernel variant (read once per process): HCP_FWD_NAMED_BARRIERS=1
-// selects the MMA issuer that meets the softmax warpgroups at named barriers
-// only (1); HCP_FWD_POLY_EXP2=1 the same with a quarter of the exponentials
-// on the FMA pipe (2); otherwise the mbarrier issuer (0).
+// Forward kernel variant (read once per process): HCP_FWD_VARIANT=0..5, or
+// HCP_FWD_NAMED_BARRIERS=1 (1) / HCP_FWD_POLY_EXP2=1 (2).  0 - the mbarrier
+// MMA issuer; 1 - the named-barrier issuer; 2 - 1 with a quarter of the
+// exponentials on the FMA pipe; 3, 4, 5 - the mbarrier issuer on 384 threads
+// with the registers split by setmaxnreg and packed f32x2 softmax math, with
+// a quarter, three eighths or none of the exponentials on the FMA pipe.
 int fwd_variant() {
   static const int v = [] {
     auto on = [](const char* name) {
       const char* e = std::getenv(name);
       return e != nullptr && e[0] == '1';
     };
+    const char* e = std::getenv("HCP_FWD_VARIANT");
+    if (e != nullptr && e[0] >= '0' && e[0] <= '5' && e[1] == 0) return e[0] - '0';
     return on("HCP_FWD_POLY_EXP2") ? 2 : on("HCP_FWD_NAMED_BARRIERS") ? 1 : 0;
   }();
   return v;
@@ -133,10 +137,18 @@ int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
       if (cudaFuncSetAttribute(ring_fwd_kernel<D, F16, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem) != cudaSuccess)
         return HCP_ERR_CUDA;
+      if (V >= 3) {
+        // setmaxnreg.inc waits until the other warpgroups have released what
+        // it asks for: the split must fit the registers the launch holds
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, ring_fwd_kernel<D, F16, V>) != cudaSuccess) return HCP_ERR_CUDA;
+        if (2 * 128 * kRegsSoftmaxWide + 128 * kRegsProducerWide > kThreadsWide * fa.numRegs)
+          return HCP_ERR_UNSUPPORTED;
+      }
       done = true;
     }
   }
-  ring_fwd_kernel<D, F16, V><<<grid, kThreads, smem, st>>>(p);
+  ring_fwd_kernel<D, F16, V><<<grid, V >= 3 ? kThreadsWide : kThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
@@ -145,6 +157,9 @@ int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
   switch (fwd_variant()) {
     case 1: return launch_fwd<D, F16, 1>(p, grid, st);
     case 2: return launch_fwd<D, F16, 2>(p, grid, st);
+    case 3: return launch_fwd<D, F16, 3>(p, grid, st);
+    case 4: return launch_fwd<D, F16, 4>(p, grid, st);
+    case 5: return launch_fwd<D, F16, 5>(p, grid, st);
     default: return launch_fwd<D, F16, 0>(p, grid, st);
   }
 }

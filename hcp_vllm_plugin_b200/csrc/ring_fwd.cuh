@@ -63,6 +63,12 @@ constexpr int kStages = 2;
 constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
 constexpr int kThreads = 320;
+// Variants 3-5: a third warpgroup (warps 8-11: TMA, MMA, two idle) so the
+// registers can be split by setmaxnreg - 224 for each softmax thread, 56 for
+// the producer warpgroup (2*128*224 + 128*56 = 384*168, the launch's total).
+constexpr int kThreadsWide = 384;
+constexpr int kRegsSoftmaxWide = 224;
+constexpr int kRegsProducerWide = 56;
 constexpr int kMaxWork = 160;
 constexpr int kMaxSegs = 2 * kMaxWork;   // segments of one launch's work items
 constexpr int kMaxItemSegs = HCP_MAX_ITEM_SEGMENTS;
@@ -216,6 +222,33 @@ __device__ __forceinline__ float exp2_poly(float x) {
 // Pairs of a 16-pair group whose exponentials take the FMA-pipe path
 // (kernel variant 2): one in four.
 __device__ __forceinline__ constexpr bool poly_pair(int i) { return (i & 3) == 3; }
+// The same choice for variants 3-5: one in four, three in eight, none.
+template <int V>
+__device__ __forceinline__ constexpr bool poly_pair_v(int i) {
+  return V == 3 ? (i & 3) == 3 : V == 4 ? ((i & 7) == 2 || (i & 7) == 5 || (i & 7) == 7) : false;
+}
+
+// 2^x of a pair on the FMA pipe with packed f32x2 arithmetic (the steps of
+// exp2_poly).  Inputs at or below -126 give 2^-126, not 0: such keys are
+// masked ones, whose weight next to a row's largest (>= 1) is immaterial.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float2 xc = make_float2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+  const float2 t = __fadd2_rn(xc, make_float2(kMagic, kMagic));
+  const float2 j = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+  const float2 f = __ffma2_rn(j, make_float2(-1.f, -1.f), xc);
+  float2 q = __ffma2_rn(make_float2(0.05517167f, 0.05517167f), f, make_float2(0.24261113f, 0.24261113f));
+  q = __ffma2_rn(q, f, make_float2(0.69326097f, 0.69326097f));
+  q = __ffma2_rn(q, f, make_float2(0.99992806f, 0.99992806f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 
 __device__ __forceinline__ float lg2_approx(float x) {
   float y;
@@ -276,9 +309,11 @@ struct FwdSmem {
 // 2 - as 1, with one in four exponentials of a tile on the FMA pipe
 //     (exp2_poly) instead of the MUFU unit.
 template <int D, bool F16, int V = 0>
-__global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_constant__ FwdParams p) {
-  constexpr bool NB = V >= 1;
+__global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
+    ring_fwd_kernel(const __grid_constant__ FwdParams p) {
+  constexpr bool NB = V == 1 || V == 2;
   constexpr bool kPoly = V == 2;
+  constexpr bool kWide = V >= 3;
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
   using L = FwdSmem<D>;
   constexpr int kHalves = D / 64;
@@ -399,7 +434,13 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     return (t - sg_base[s]) * kBlockN < (x == 0 ? sg_need_a[s] : sg_need_b[s]);
   };
   const bool skip_all = *abort_flag != 0;
-
+  // Each warpgroup's setmaxnreg opens its own branch (every thread of the
+  // warpgroup runs it, whatever its role or the abort state), so the code of
+  // each role is register-allocated under that warpgroup's limit.
+  if (warp >= 8) {
+  // ============================================== producer warpgroup: TMA, MMA
+  // (and, in variants 3-5, the spare warps 10-11 with no role)
+  if constexpr (kWide) ptx::setmaxnreg_dec<kRegsProducerWide>();
   if (skip_all) {
     // nothing issued, nothing to drain
   } else if (warp == kWarpTma) {
@@ -633,7 +674,10 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
     __syncwarp();
     drain_bar(b_final, 0);
     }
+  }
   } else {
+  if constexpr (kWide) ptx::setmaxnreg_inc<kRegsSoftmaxWide>();
+  if (!skip_all) {
     // ================================================================ softmax + epilogue
     const int x = warp >> 2;                 // query tile of this warpgroup (0 = A, 1 = B)
     const int quarter = warp & 3;
@@ -806,20 +850,61 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
         for (int i = 0; i < 128; ++i)
           if (i >= vis) sr[i] = __float_as_uint(-INFINITY);
       }
-      float mx8[8];
+      float mx;
+      if constexpr (kWide) {
+        float mx8[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx8[j] = __uint_as_float(sr[j]);
+        for (int j = 0; j < 8; ++j)
+          mx8[j] = max3(__uint_as_float(sr[j]), __uint_as_float(sr[j + 8]), __uint_as_float(sr[j + 16]));
 #pragma unroll
-      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int i = 24; i < 120; i += 16)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            mx8[j] = max3(mx8[j], __uint_as_float(sr[i + j]), __uint_as_float(sr[i + 8 + j]));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = fmaxf(mx8[j], __uint_as_float(sr[120 + j]));
+        mx = max3(max3(mx8[0], mx8[1], mx8[2]), max3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+      } else {
+        float mx8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx8[j] = __uint_as_float(sr[j]);
+#pragma unroll
+        for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[i]));
+        mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      }
       const float mx2 = mx * scale_log2;  // -inf stays -inf
       const bool raise = mx2 > m_used + kRescaleThreshold;
       const float m_new = raise ? mx2 : m_used;
       const float alpha = raise ? ex2_approx(m_used - m_new) : 1.f;  // 0 when m_used = -inf
       const float m_base = (m_new == -INFINITY) ? 0.f : m_new;
       float sums[4] = {0.f, 0.f, 0.f, 0.f};
-      if (!precise) {
+      if (kWide && !precise) {
+        // packed f32x2: x = s * scale - m two keys at a time, sums likewise;
+        // a share of the exponentials on the FMA pipe (poly_pair_v)
+        const float2 sc2 = make_float2(scale_log2, scale_log2);
+        const float2 mb2 = make_float2(-m_base, -m_base);
+        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 sv = make_float2(__uint_as_float(sr[c * 32 + 2 * i]), __uint_as_float(sr[c * 32 + 2 * i + 1]));
+            const float2 xx = __ffma2_rn(sv, sc2, mb2);
+            float2 pp;
+            if (poly_pair_v<V>(i)) pp = exp2_poly2(xx);
+            else pp = make_float2(ex2_approx(xx.x), ex2_approx(xx.y));
+            acc2[i & 1] = __fadd2_rn(acc2[i & 1], pp);
+            pk[i] = pack2<F16>(pp.x, pp.y);
+          }
+          ptx::tmem_st_32x32b_x16(s_addr + c * 16, pk);
+        }
+        sums[0] = acc2[0].x;
+        sums[1] = acc2[0].y;
+        sums[2] = acc2[1].x;
+        sums[3] = acc2[1].y;
+      } else if (!precise) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
@@ -964,6 +1049,7 @@ __global__ void __launch_bounds__(kThreads, 1) ring_fwd_kernel(const __grid_cons
       }
       if (valid && p.lse != nullptr) p.lse[head * p.lse_stride + lse_idx_col] = lse_v;
     }
+  }
   }
 
   // ---- teardown: release TMEM once every role is done with it
