@@ -422,16 +422,27 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   const int n_seg = sg_misc[0];
   const int n_tiles = sg_base[n_seg];
   const bool precise_a = sg_misc[1] != 0, precise_b = sg_misc[2] != 0;
+  // Items of one or two segments (every inline item) keep their table in
+  // registers: these lookups sit on the MMA issuer's per-tile path.  Longer
+  // lists walk the shared-memory table.
+  const bool few = n_seg <= 2;
+  const int t1 = n_seg >= 2 ? sg_base[1] : n_tiles;  // first tile of segment 1
+  const int need_a0 = sg_need_a[0], need_b0 = sg_need_b[0];
+  const int need_a1 = sg_need_a[1], need_b1 = sg_need_b[1];
   auto tile_seg = [&](int t) {
+    if (few) return t < t1 ? 0 : 1;
     int s = 0;
     while (s + 1 < n_seg && t >= sg_base[s + 1]) ++s;
     return s;
   };
-  auto tile_key0 = [&](int t) { return (t - sg_base[tile_seg(t)]) * kBlockN; };
+  auto seg_base = [&](int s) { return few ? (s == 0 ? 0 : t1) : sg_base[s]; };
+  auto tile_key0 = [&](int t) { return (t - seg_base(tile_seg(t))) * kBlockN; };
   // is KV tile t needed by query tile x (0 = A, 1 = B)?
   auto active = [&](int x, int t) {
     const int s = tile_seg(t);
-    return (t - sg_base[s]) * kBlockN < (x == 0 ? sg_need_a[s] : sg_need_b[s]);
+    const int need = few ? (s == 0 ? (x == 0 ? need_a0 : need_b0) : (x == 0 ? need_a1 : need_b1))
+                         : (x == 0 ? sg_need_a[s] : sg_need_b[s]);
+    return (t - seg_base(s)) * kBlockN < need;
   };
   const bool skip_all = *abort_flag != 0;
   // Each warpgroup's setmaxnreg opens its own branch (every thread of the
