@@ -429,6 +429,11 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   const int t1 = n_seg >= 2 ? sg_base[1] : n_tiles;  // first tile of segment 1
   const int need_a0 = sg_need_a[0], need_b0 = sg_need_b[0];
   const int need_a1 = sg_need_a[1], need_b1 = sg_need_b[1];
+  // the segments themselves too: a load through the item's segment pointer
+  // on every tile would sit on the softmax and producer paths
+  const hcp_kv_segment seg_r0 = segs[0];
+  const hcp_kv_segment seg_r1 = n_seg > 1 ? segs[1] : seg_r0;
+  auto seg_at = [&](int s) -> hcp_kv_segment { return few ? (s == 0 ? seg_r0 : seg_r1) : segs[s]; };
   auto tile_seg = [&](int t) {
     if (few) return t < t1 ? 0 : 1;
     int s = 0;
@@ -468,7 +473,7 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
       const int s = t % kStages;
       const uint32_t ph = (t / kStages) & 1;
       const int key0 = tile_key0(t);
-      const hcp_kv_segment& seg = segs[tile_seg(t)];
+      const hcp_kv_segment seg = seg_at(tile_seg(t));
       const uint32_t s_k = s_kv0 + (2 * s) * kTileBytes;
       const uint32_t s_v = s_k + kTileBytes;
       int blk_ids[8];
@@ -729,7 +734,7 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
       if (ok) {
         ptx::tc_fence_after();
         const int key0 = tile_key0(t);
-        const hcp_kv_segment& seg = segs[tile_seg(t)];
+        const hcp_kv_segment seg = seg_at(tile_seg(t));
         int vis = seg.len - key0;
         if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
         vis = max(0, min(vis, kBlockN));
@@ -846,7 +851,7 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
       if (!ok) break;
       ptx::tc_fence_after();
       const int key0 = tile_key0(t);
-      const hcp_kv_segment& seg = segs[tile_seg(t)];
+      const hcp_kv_segment seg = seg_at(tile_seg(t));
       int vis = seg.len - key0;
       if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
       vis = max(0, min(vis, kBlockN));
