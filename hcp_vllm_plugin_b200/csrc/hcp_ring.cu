@@ -103,7 +103,7 @@ bool encode_rows_heads(CUtensorMap* m, bool f16, const void* base, int64_t rows,
 }
 
 std::mutex g_attr_mu;
-bool g_attr_done[2][2][6][64];
+bool g_attr_done[2][2][7][64];  // variants 0-5, and 6 for the LIST kernel
 bool g_dec_attr_done[2][2][64];
 
 // Forward kernel variant (read once per process): HCP_FWD_VARIANT=0..5, or
@@ -125,35 +125,37 @@ int fwd_variant() {
   return v;
 }
 
-template <int D, bool F16, int V>
+template <int D, bool F16, int V, bool LIST = false>
 int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
   constexpr int smem = fwd_smem_bytes<D>();
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
-    bool& done = g_attr_done[D == 128][F16][V][dev];
+    bool& done = g_attr_done[D == 128][F16][LIST ? 6 : V][dev];
     if (!done) {
-      if (cudaFuncSetAttribute(ring_fwd_kernel<D, F16, V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      if (cudaFuncSetAttribute(ring_fwd_kernel<D, F16, V, LIST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem) != cudaSuccess)
         return HCP_ERR_CUDA;
       if (V >= 3) {
         // setmaxnreg.inc waits until the other warpgroups have released what
         // it asks for: the split must fit the registers the launch holds
         cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, ring_fwd_kernel<D, F16, V>) != cudaSuccess) return HCP_ERR_CUDA;
+        if (cudaFuncGetAttributes(&fa, ring_fwd_kernel<D, F16, V, LIST>) != cudaSuccess) return HCP_ERR_CUDA;
         if (2 * 128 * kRegsSoftmaxWide + 128 * kRegsProducerWide > kThreadsWide * fa.numRegs)
           return HCP_ERR_UNSUPPORTED;
       }
       done = true;
     }
   }
-  ring_fwd_kernel<D, F16, V><<<grid, V >= 3 ? kThreadsWide : kThreads, smem, st>>>(p);
+  ring_fwd_kernel<D, F16, V, LIST><<<grid, V >= 3 ? kThreadsWide : kThreads, smem, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
 template <int D, bool F16>
-int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
+int launch_fwd(const FwdParams& p, int grid, cudaStream_t st, bool list) {
+  // items of more than two segments: the segment-table kernel (mbarrier issuer)
+  if (list) return launch_fwd<D, F16, 0, true>(p, grid, st);
   switch (fwd_variant()) {
     case 1: return launch_fwd<D, F16, 1>(p, grid, st);
     case 2: return launch_fwd<D, F16, 2>(p, grid, st);
@@ -315,6 +317,7 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
           w.seg[0].len > HCP_MAX_ITEM_SEGMENTS || static_cast<int64_t>(w.seg[0].start) + w.seg[0].len > a->num_seg_list)
         return HCP_ERR_INVALID;
       sg.assign(a->seg_list + w.seg[0].start, a->seg_list + w.seg[0].start + w.seg[0].len);
+      while (sg.size() < 2) sg.push_back(hcp_kv_segment{HCP_SRC_NONE, 0, 0, 0});
     } else {
       sg.assign(w.seg, w.seg + 2);
     }
@@ -393,11 +396,13 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
   for (size_t base = 0; base < order.size();) {
     // one launch: up to kMaxWork items whose segments fit kMaxSegs
     int n = 0, nseg = 0, tiles = 0;
+    bool list = false;
     while (base + n < order.size() && n < kMaxWork) {
       const int idx = order[base + n];
       const auto& sg = item_segs[idx];
       if (nseg + static_cast<int>(sg.size()) > kMaxSegs) break;
       const hcp_attn_work& w = items[idx];
+      list = list || sg.size() > 2;
       FwdItem& it = p.work[n];
       it.q_start = w.q_start;
       it.q_len = w.q_len;
@@ -418,10 +423,10 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
     if (grid <= 0) continue;
     if (grid > 0x7fffffff) return HCP_ERR_UNSUPPORTED;
     int rc;
-    if (D == 128) rc = f16 ? launch_fwd<128, true>(p, static_cast<int>(grid), st)
-                           : launch_fwd<128, false>(p, static_cast<int>(grid), st);
-    else rc = f16 ? launch_fwd<64, true>(p, static_cast<int>(grid), st)
-                  : launch_fwd<64, false>(p, static_cast<int>(grid), st);
+    if (D == 128) rc = f16 ? launch_fwd<128, true>(p, static_cast<int>(grid), st, list)
+                           : launch_fwd<128, false>(p, static_cast<int>(grid), st, list);
+    else rc = f16 ? launch_fwd<64, true>(p, static_cast<int>(grid), st, list)
+                  : launch_fwd<64, false>(p, static_cast<int>(grid), st, list);
     if (rc != HCP_OK) return rc;
   }
   return HCP_OK;

@@ -308,7 +308,11 @@ struct FwdSmem {
 //     mbarrier waits for the tiles their P feeds (see below);
 // 2 - as 1, with one in four exponentials of a tile on the FMA pipe
 //     (exp2_poly) instead of the MUFU unit.
-template <int D, bool F16, int V = 0>
+// LIST: items may have more than two segments (a per-CTA segment table in
+// shared memory).  Without it every item has exactly two segments, which each
+// thread keeps in registers: the per-tile lookups sit on the MMA issuer's and
+// the softmax warps' paths, and a table read there was measured 25% slower.
+template <int D, bool F16, int V = 0, bool LIST = false>
 __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
     ring_fwd_kernel(const __grid_constant__ FwdParams p) {
   constexpr bool NB = V == 1 || V == 2;
@@ -361,17 +365,34 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   const int q0 = m_blk * kCtaRows;
   const int rows_a = max(0, min(kBlockM, wk.q_len - q0));
   const int rows_b = max(0, min(kBlockM, wk.q_len - q0 - kBlockM));
-  // The CTA's segment table (shared memory, filled by thread 0 at setup):
-  // the KV tiles of segment s are [sg_base[s], sg_base[s+1]); query tile A
-  // needs its first sg_need_a[s] keys, B its first sg_need_b[s].
+  // Two-segment items: every thread's own copy of the table, in registers.
+  hcp_kv_segment sg0{}, sg1{};
+  int ka0 = 0, kb0 = 0, ka1 = 0, kb1 = 0, tiles0 = 0, tiles2 = 0;
+  bool pre_a = false, pre_b = false;
+  if constexpr (!LIST) {
+    sg0 = segs[0];
+    sg1 = segs[1];
+    ka0 = segment_keys(sg0, q0, rows_a);
+    kb0 = segment_keys(sg0, q0 + kBlockM, rows_b);
+    ka1 = segment_keys(sg1, q0, rows_a);
+    kb1 = segment_keys(sg1, q0 + kBlockM, rows_b);
+    tiles0 = (max(ka0, kb0) + kBlockN - 1) / kBlockN;
+    tiles2 = tiles0 + (max(ka1, kb1) + kBlockN - 1) / kBlockN;
+    // Rows that see few keys in total get P as hi + lo 16-bit parts.
+    pre_a = segment_keys(sg0, q0, 1) + segment_keys(sg1, q0, 1) < kPreciseKeys;
+    pre_b = segment_keys(sg0, q0 + kBlockM, 1) + segment_keys(sg1, q0 + kBlockM, 1) < kPreciseKeys;
+  }
+  // LIST: the CTA's segment table (shared memory, filled by thread 0 at
+  // setup): the KV tiles of segment s are [sg_base[s], sg_base[s+1]); query
+  // tile A needs its first sg_need_a[s] keys, B its first sg_need_b[s].
   int* sg_base = reinterpret_cast<int*>(smem + L::kSegOff);
   int* sg_need_a = sg_base + kMaxItemSegs + 1;
   int* sg_need_b = sg_need_a + kMaxItemSegs;
   int* sg_misc = sg_need_b + kMaxItemSegs;  // [0] segments, [1] precise A, [2] precise B
 
   // ---- setup
-  if (threadIdx.x == 0) {
-    // keys each query tile needs from each segment; the KV tile list covers both
+  if (LIST && threadIdx.x == 0) {
+    // keys each query tile needs from each segment; the KV tile list covers all
     int tiles = 0, keys_a = 0, keys_b = 0;
     const int n_seg = min(wk.seg_count, kMaxItemSegs);
     for (int s = 0; s < n_seg; ++s) {
@@ -388,6 +409,8 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
     // Rows that see few keys in total get P as hi + lo 16-bit parts.
     sg_misc[1] = keys_a < kPreciseKeys;
     sg_misc[2] = keys_b < kPreciseKeys;
+  }
+  if (threadIdx.x == 0) {
     ptx::mbar_init(b_q, 1);
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(b_kfull(s), 1);
@@ -419,34 +442,34 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int n_seg = sg_misc[0];
-  const int n_tiles = sg_base[n_seg];
-  const bool precise_a = sg_misc[1] != 0, precise_b = sg_misc[2] != 0;
-  // Items of one or two segments (every inline item) keep their table in
-  // registers: these lookups sit on the MMA issuer's per-tile path.  Longer
-  // lists walk the shared-memory table.
-  const bool few = n_seg <= 2;
-  const int t1 = n_seg >= 2 ? sg_base[1] : n_tiles;  // first tile of segment 1
-  const int need_a0 = sg_need_a[0], need_b0 = sg_need_b[0];
-  const int need_a1 = sg_need_a[1], need_b1 = sg_need_b[1];
-  // the segments themselves too: a load through the item's segment pointer
-  // on every tile would sit on the softmax and producer paths
-  const hcp_kv_segment seg_r0 = segs[0];
-  const hcp_kv_segment seg_r1 = n_seg > 1 ? segs[1] : seg_r0;
-  auto seg_at = [&](int s) -> hcp_kv_segment { return few ? (s == 0 ? seg_r0 : seg_r1) : segs[s]; };
+  const int n_seg = LIST ? sg_misc[0] : 2;
+  const int n_tiles = LIST ? sg_base[n_seg] : tiles2;
+  const bool precise_a = LIST ? sg_misc[1] != 0 : pre_a;
+  const bool precise_b = LIST ? sg_misc[2] != 0 : pre_b;
   auto tile_seg = [&](int t) {
-    if (few) return t < t1 ? 0 : 1;
-    int s = 0;
-    while (s + 1 < n_seg && t >= sg_base[s + 1]) ++s;
-    return s;
+    if constexpr (!LIST) {
+      return t < tiles0 ? 0 : 1;
+    } else {
+      int s = 0;
+      while (s + 1 < n_seg && t >= sg_base[s + 1]) ++s;
+      return s;
+    }
   };
-  auto seg_base = [&](int s) { return few ? (s == 0 ? 0 : t1) : sg_base[s]; };
+  auto seg_base = [&](int s) {
+    if constexpr (!LIST) return s == 0 ? 0 : tiles0;
+    else return sg_base[s];
+  };
+  auto seg_at = [&](int s) -> hcp_kv_segment {
+    if constexpr (!LIST) return s == 0 ? sg0 : sg1;
+    else return segs[s];
+  };
   auto tile_key0 = [&](int t) { return (t - seg_base(tile_seg(t))) * kBlockN; };
   // is KV tile t needed by query tile x (0 = A, 1 = B)?
   auto active = [&](int x, int t) {
     const int s = tile_seg(t);
-    const int need = few ? (s == 0 ? (x == 0 ? need_a0 : need_b0) : (x == 0 ? need_a1 : need_b1))
-                         : (x == 0 ? sg_need_a[s] : sg_need_b[s]);
+    int need;
+    if constexpr (!LIST) need = s == 0 ? (x == 0 ? ka0 : kb0) : (x == 0 ? ka1 : kb1);
+    else need = x == 0 ? sg_need_a[s] : sg_need_b[s];
     return (t - seg_base(s)) * kBlockN < need;
   };
   const bool skip_all = *abort_flag != 0;
