@@ -206,7 +206,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // x = j + f with j = rint(x) by the 1.5 * 2^23 rounding trick (f in
 // [-1/2, 1/2]); 2^f by a degree-3 polynomial, minimax in relative error on
 // that interval (Remez exchange; coefficients and their 7.5e-5 error from
-// gen_exp2_poly.py); 2^j by adding j to the exponent bits: the low bits of
+// tests/gen_exp2_poly.py); 2^j by adding j to the exponent bits: the low bits of
 // the rounded float hold j, and shifting them by 23 drops the rest.  At or
 // below -126 the result is 0, as ex2.approx.ftz gives for masked keys.
 __device__ __forceinline__ float exp2_poly(float x) {

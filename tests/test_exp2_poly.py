@@ -1,6 +1,6 @@
 """The forward kernel's FMA-pipe exponential (``exp2_poly`` in
 ``csrc/ring_fwd.cuh``, variant 2): its coefficients are the ones the Remez
-exchange in ``csrc/gen_exp2_poly.py`` derives, and the device steps, emulated
+exchange in ``tests/gen_exp2_poly.py`` derives, and the device steps, emulated
 in float32 here, stay within 1e-4 relative error of 2**x on (-126, 0] (the
 bf16 P it feeds is rounded to 2**-9) and give exactly 0 at or below -126 and
 for masked keys (-inf), as ``ex2.approx.ftz`` does."""
@@ -42,7 +42,7 @@ def exp2_poly(x):
 
 
 def test_coefficients_are_the_remez_solution():
-    spec = importlib.util.spec_from_file_location("gen_exp2_poly", os.path.join(CSRC, "gen_exp2_poly.py"))
+    spec = importlib.util.spec_from_file_location("gen_exp2_poly", os.path.join(ROOT, "tests", "gen_exp2_poly.py"))
     gen = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(gen)
     c, err = gen.remez_exp2()

@@ -1,7 +1,12 @@
-"""The forward kernel's named-barrier MMA issuer (``HCP_FWD_NAMED_BARRIERS=1``)
-must give the same answers as the default issuer: the whole forward parity
-suite (``test_fwd_gpu.py``) runs again in a child process with the switch
-set (the library reads it once per process)."""
+"""Every opt-in variant of the forward kernel must give the default's
+answers: the forward parity suite (``test_fwd_gpu.py``, without its
+131072-token case) runs again in a child process per variant, the variant
+chosen by ``HCP_FWD_VARIANT`` (the library reads it once per process).
+
+1 - named-barrier MMA issuer; 2 - 1 with a quarter of the exponentials on
+the FMA pipe; 3, 4, 5 - 384 threads with the registers split by setmaxnreg
+and packed softmax math, with a quarter, three eighths or none of the
+exponentials on the FMA pipe."""
 
 import os
 import subprocess
@@ -13,10 +18,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.gpu
-def test_named_barrier_issuer_passes_the_forward_parity_suite():
-    env = dict(os.environ, HCP_FWD_NAMED_BARRIERS="1")
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5"])
+def test_forward_variant_passes_the_forward_parity_suite(variant):
+    env = dict(os.environ, HCP_FWD_VARIANT=variant)
     cmd = [sys.executable, "-m", "pytest", os.path.join(HERE, "test_fwd_gpu.py"), "-q", "-x", "-m", "gpu",
-           "-p", "no:cacheprovider"]
+           "-k", "not cfg3", "-p", "no:cacheprovider"]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600, cwd=os.path.dirname(HERE))
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
     assert " passed" in r.stdout and "failed" not in r.stdout
