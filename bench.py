@@ -14,8 +14,10 @@ Prints one JSON line on rank 0.  ``value`` is whole-job tokens/s measured on
 the device (CUDA events, barrier + synchronize around the timed steps, max
 over ranks).  ``e2e`` repeats the measurement through the public API with
 every layer's q/k/v copied from pinned host memory and the output copied
-back.  ``--impl reference`` times the reference algorithm's CPU path (the
-oracle port of its fp32 torch path) on a bounded sample and extrapolates.
+back.  ``--impl reference`` times the reference's own fp32 torch attention
+(``_attn_with_lse`` from the installed reference package, else the oracle's
+numpy restatement of it) on the host cores over a bounded sample of the same
+step and extrapolates by FLOPs (``"extrapolated": true``).
 """
 
 from __future__ import annotations
@@ -113,56 +115,103 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_sample(seq: int, rows: int, seed: int = 0):
-    """Time the oracle (the reference's fp32 torch algorithm restated in numpy)
-    on the last ``rows`` query rows of one layer (each sees ~``seq`` keys).
-    Returns (seconds, flops of the sample, threads)."""
-    import numpy as np
+def _reference_attn():
+    """The reference plugin's own fp32 torch ``_attn_with_lse``
+    (``hcp_vllm_plugin/ring_backend.py:366-406``) from ``baseline/_ref``, or
+    None when the package is not installed there."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "hcp_vllm_plugin")):
+        return None
+    if ref not in sys.path:
+        sys.path.append(ref)
+    try:
+        from hcp_vllm_plugin.ring_backend import _attn_with_lse
+    except Exception:  # noqa: BLE001 - fall back to the port
+        return None
+    return _attn_with_lse
 
-    from oracle import ring_oracle as ro
+
+REF_BLOCK = 128
+
+
+def cpu_rows(args) -> int:
+    """Query rows of one CPU sample: the reference's torch path reaches its
+    steady rate only in blocks of 128 rows, the port in 32-row blocks."""
+    if args.cpu_rows:
+        return args.cpu_rows
+    return 2 * REF_BLOCK if _reference_attn() is not None else 448
+
+
+def cpu_sample(seq: int, rows: int, seed: int = 0):
+    """Time the reference's CPU path on the last ``rows`` query rows of one
+    layer (each sees ~``seq`` keys): its own ``_attn_with_lse`` on the host
+    cores when installed (kind "reference"), else the oracle's numpy
+    restatement of it (kind "port").  Rows go 128 (32 for the port) at a
+    time, since the reference materialises the [H, rows, keys] fp32 scores
+    (1.9 GB at 128 rows x 128k keys).  Returns (seconds, flops of the sample,
+    threads, kind)."""
+    import numpy as np
 
     rng = np.random.default_rng(seed)
     q = rng.standard_normal((rows, H, D), dtype=np.float32)
     k = rng.standard_normal((seq, HKV, D), dtype=np.float32)
     v = rng.standard_normal((seq, HKV, D), dtype=np.float32)
+    flops = 4.0 * D * H * sum(seq - rows + i + 1 for i in range(rows))
+    attn = _reference_attn()
+    if attn is not None:
+        import torch
+
+        qt, kt, vt = (torch.from_numpy(a).to(torch.bfloat16) for a in (q, k, v))
+        t0 = time.perf_counter()
+        for r0 in range(0, rows, REF_BLOCK):
+            attn(qt[r0:r0 + REF_BLOCK], kt, vt, D ** -0.5, seq - rows + r0)
+        return time.perf_counter() - t0, flops, torch.get_num_threads(), "reference"
+    from oracle import ring_oracle as ro
+
     q, k, v = ro.round_bf16(q), ro.round_bf16(k), ro.round_bf16(v)
     t0 = time.perf_counter()
     ro.attn_with_lse(q, k, v, D ** -0.5, seq - rows, q_block=min(rows, 32))  # ~0.5 GB of scores at a time
     dt = time.perf_counter() - t0
-    flops = 4.0 * D * H * ro.visible_pairs(rows, seq, seq - rows)
     try:
         from threadpoolctl import threadpool_info
         threads = max([x.get("num_threads", 1) for x in threadpool_info()] or [1])
     except Exception:  # noqa: BLE001
         threads = os.cpu_count() or 1
-    return dt, flops, threads
+    return dt, flops, threads, "port"
+
+
+def _sample_text(kind: str, rows: int, seq: int, layers: int, secs: float) -> str:
+    what = ("the reference's own fp32 torch _attn_with_lse (ring_backend.py:366-406)" if kind == "reference"
+            else "fp32 numpy oracle port of ring_backend.py:366-406")
+    return (f"one layer, last {rows} query rows x {seq} keys causal, 28 heads, {what}: {secs:.2f} s, "
+            f"extrapolated by FLOPs to the whole {seq}-token x {layers}-layer step")
 
 
 def run_reference(args, rank):
     if rank != 0:
         return
     seq, layers = args.seq, args.layers
-    rows = args.cpu_rows
+    rows = cpu_rows(args)
     total = step_flops(seq, layers)
-    for _ in range(args.warmup):  # untimed: warms the BLAS threads and the allocator
-        cpu_sample(seq, min(rows, 32))
-    rates = []
-    threads = 1
+    for _ in range(args.warmup):  # untimed: first-touch of the ~8 GB of fp32 buffers, BLAS threads
+        cpu_sample(seq, min(rows, REF_BLOCK))
+    rates, secs = [], []
+    threads, kind = 1, "port"
     for _ in range(args.steps):
-        dt, fl, threads = cpu_sample(seq, rows)
+        dt, fl, threads, kind = cpu_sample(seq, rows)
         rates.append(fl / dt)
+        secs.append(dt)
     rate = statistics.median(rates)
     tok_s = seq / (total / rate)
-    sample = (f"one layer, last {rows} query rows x {seq} keys causal, 28 heads, fp32 numpy "
-              f"(oracle port of ring_backend.py:366-406), extrapolated by FLOPs to {layers} layers")
     line = {
         "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / rate, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config(args), "tflops": rate / 1e12,
-        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+        "extrapolated": True, "sample_seconds": secs,
+        "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": kind,
+                         "sample": _sample_text(kind, rows, seq, layers, statistics.median(secs))},
         "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -184,7 +233,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seq", type=int, default=131072)
     ap.add_argument("--layers", type=int, default=28)
-    ap.add_argument("--cpu-rows", type=int, default=448)  # ~10 s of oracle work on 16 cores
+    ap.add_argument("--cpu-rows", type=int, default=0)  # 0: 256 (reference) / 448 (port), ~10 s each
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-balance", action="store_true")
@@ -342,12 +391,12 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        dt, fl, threads = cpu_sample(seq, args.cpu_rows)
+        cpu_sample(seq, min(cpu_rows(args), REF_BLOCK))  # untimed first touch
+        dt, fl, threads, kind = cpu_sample(seq, cpu_rows(args))
         rate = fl / dt
         cpu = {"value": seq / (step_flops(seq, L) / rate), "unit": "tok/s", "cores": threads,
-               "kind": "port",
-               "sample": f"one layer, last {args.cpu_rows} query rows x {seq} keys causal, fp32 "
-                         f"numpy oracle, {dt:.2f} s, extrapolated by FLOPs to {L} layers"}
+               "kind": kind, "extrapolated": True,
+               "sample": _sample_text(kind, cpu_rows(args), seq, L, dt)}
 
     if rank == 0:
         line = {
