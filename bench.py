@@ -650,16 +650,19 @@ def reference_gpu_side(dev, pk) -> dict:
 
 
 def fwd_issuer_variants(seq: int) -> dict:
-    """The forward kernel on one ``seq``-token causal launch in each variant:
-    the default (mbarrier) MMA issuer, the named-barrier issuer
-    (``HCP_FWD_NAMED_BARRIERS=1``) and the named-barrier issuer with a quarter
-    of the exponentials on the FMA pipe (``HCP_FWD_POLY_EXP2=1``), each in a
-    fresh process, since the library reads the switches once per process.
-    Reported beside the headline only."""
+    """The forward kernel on one ``seq``-token causal launch in each variant
+    (``HCP_FWD_VARIANT``): 0 the default mbarrier MMA issuer, 1 the
+    named-barrier issuer, 2 variant 1 with a quarter of the exponentials on
+    the FMA pipe, 3-5 the mbarrier issuer on 384 threads with setmaxnreg
+    register split and packed f32x2 softmax math, with 1/4, 3/8 and none of
+    the exponentials on the FMA pipe.  Each runs in a fresh process, since the
+    library reads the switch once per process.  Reported beside the headline
+    only."""
     out = {}
-    for name, nb, poly in (("mbarrier_issuer", "0", "0"), ("named_barrier_issuer", "1", "0"),
-                           ("named_barrier_poly_exp2", "1", "1")):
-        env = dict(os.environ, HCP_FWD_NAMED_BARRIERS=nb, HCP_FWD_POLY_EXP2=poly)
+    names = ("mbarrier_issuer", "named_barrier_issuer", "named_barrier_poly_exp2",
+             "wide_poly_quarter", "wide_poly_three_eighths", "wide_no_poly")
+    for variant, name in enumerate(names):
+        env = dict(os.environ, HCP_FWD_VARIANT=str(variant))
         cmd = [sys.executable, os.path.abspath(__file__), "--kernel", "fwd", "--seq", str(seq), "--iters", "5"]
         try:
             r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=180)

@@ -21,7 +21,9 @@ Semantics kept from the reference (``hcp_vllm_plugin/ring_connector.py``):
   layers ahead of ``wait_for_layer_load`` and frees the staging of layers
   already consumed (``:144-170, 794-888``); chunks are refcounted across
   requests and freed when the last user finishes, before the step that may
-  recycle its blocks (``:240-250, 939-997``).
+  recycle its blocks (``:240-250, 939-997``).  That bookkeeping lives in
+  ``staging_ledger`` (chunk holds, the per-request layer feed, ready-marker
+  lookups, decode-ring slots).
 
 What changes is the transport.  The reference producer writes one
 safetensors file per layer and serves its store over HTTP; a consumer
@@ -65,13 +67,11 @@ from . import ops
 from .ring_backend import (
     PEER_KV_STAGING,
     clear_decode_ring,
-    drop_chunk_kv,
-    map_request_peer,
     register_decode_ring,
     set_staging_release_fn,
     stage_peer_kv,
-    unmap_request_peer,
 )
+from .staging_ledger import ChunkLedger, DecodeSlotPool, LayerFeed, ReadinessCache
 
 if TYPE_CHECKING:
     from vllm.config import VllmConfig
@@ -217,23 +217,6 @@ class ChunkSource:
             self._base = None
 
 
-class _PrefillStream:
-    """One request's staging pipeline: per-layer readiness, the consumption
-    watermark, and the first error."""
-
-    def __init__(self, req_id: str, layers: list[str], chunks: list[str], expected_total: int):
-        self.req_id = req_id
-        self.layers = layers
-        self.chunks = chunks
-        self.expected_total = expected_total
-        self.events = {ln: threading.Event() for ln in layers}
-        self.cuda_events: dict[str, Any] = {}
-        self.consumed_idx = -1
-        self.error: BaseException | None = None
-        self.done = threading.Event()
-        self.thread: threading.Thread | None = None
-
-
 class HcpRingKvConnector(KVConnectorBase_V1):
     """Ring-KV connector: external-prefix scheduling + transient NVLink staging."""
 
@@ -298,18 +281,15 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         # reference's bulk staging when the decode ring is off).
         self._drop_consumed = self._decode_on
         self._decode_ring = None
-        self._decode_free_slots = list(range(self._decode_slots))
-        self._decode_slot_of: dict[str, tuple[int, int]] = {}   # req -> (slot, first block id)
+        self._slots = DecodeSlotPool(self._decode_slots)
         self._decode_stop = threading.Event()
         self._decode_thread: threading.Thread | None = None
         self._decode_error: BaseException | None = None
-        self._ready_ok: set[str] = set()
-        self._ready_next_poll: dict[str, float] = {}
+        self._readiness = ReadinessCache(self._poll_interval)
         self._requests_need_load: dict[str, Any] = {}
         # worker-side bookkeeping
-        self._live: dict[str, tuple[int, list[str]]] = {}
-        self._chunk_refs: dict[str, int] = {}
-        self._streams: dict[str, _PrefillStream] = {}
+        self._ledger = ChunkLedger()
+        self._feeds: dict[str, LayerFeed] = {}
         self._sources: dict[str, Any] = {}
         self._stage_lock = threading.Lock()
         self._side_stream = None
@@ -371,11 +351,7 @@ class HcpRingKvConnector(KVConnectorBase_V1):
     def _register_decode(self, req: "RingReqMeta", expected: int, device: torch.device) -> None:
         if self._decode_ring is None:
             self._decode_ring = self._make_decode_ring(device)
-        if not self._decode_free_slots:
-            raise RuntimeError(f"HcpRingKvConnector: all {self._decode_slots} decode ring slots are in use "
-                               "(ring_decode_slots)")
-        slot = self._decode_free_slots.pop(0)
-        self._decode_slot_of[req.req_id] = (slot, req.first_block_id)
+        slot = self._slots.take(req.req_id, req.first_block_id)
         register_decode_ring(req.first_block_id, self._decode_ring, slot, expected)
 
     # ------------------------------------------------------------------ paths
@@ -390,17 +366,7 @@ class HcpRingKvConnector(KVConnectorBase_V1):
 
     # ------------------------------------------------------------------ scheduler side
     def _prefix_ready(self, chunk_key: str) -> bool:
-        if chunk_key in self._ready_ok:
-            return True
-        now = time.monotonic()
-        if now < self._ready_next_poll.get(chunk_key, 0.0):
-            return False
-        ok = os.path.exists(self._ready_marker(chunk_key))
-        if ok:
-            self._ready_ok.add(chunk_key)
-        else:
-            self._ready_next_poll[chunk_key] = now + self._poll_interval
-        return ok
+        return self._readiness.is_ready(chunk_key, self._ready_marker(chunk_key))
 
     def get_num_new_matched_tokens(self, request: "Request",
                                    num_computed_tokens: int) -> tuple[int | None, bool]:
@@ -467,49 +433,35 @@ class HcpRingKvConnector(KVConnectorBase_V1):
             self._sources[chunk_key] = src
         return src
 
-    def _stream_worker(self, st: _PrefillStream, device: torch.device) -> None:
-        window = stream_window()
-        try:
-            if device.type == "cuda":
-                torch.cuda.set_device(device)
-            lens: dict[str, int] = {}
-            for i, layer_name in enumerate(st.layers):
-                while not st.done.is_set() and st.consumed_idx < i - window:
-                    time.sleep(0.0005)
-                if st.done.is_set():
-                    return
-                for ck in st.chunks:
-                    with self._stage_lock:
-                        staged = PEER_KV_STAGING.get((ck, layer_name))
-                        if staged is not None:
-                            lens[ck] = int(staged[0].shape[0])
-                            continue
-                        src = self._source(ck, device)
-                        _, _, t, hkv, d = src.shape
-                        if device.type == "cuda":
-                            with torch.cuda.stream(self._side_stream):
-                                k = torch.empty(t, hkv, d, dtype=src.dtype, device=device)
-                                v = torch.empty_like(k)
-                                src.copy_layer(layer_index(layer_name), k, v, self._side_stream)
-                        else:
-                            k = torch.empty(t, hkv, d, dtype=src.dtype, device=device)
-                            v = torch.empty_like(k)
-                            src.copy_layer(layer_index(layer_name), k, v, None)
-                        stage_peer_kv(ck, layer_name, k, v)
-                        lens[ck] = t
+    def _stage_layer(self, chunks: list[str], layer_name: str, device: torch.device):
+        """Stage every chunk of ``chunks`` for ``layer_name`` (once per chunk
+        and layer, whichever request asks first); returns the chunks' token
+        counts and an event on the side stream after the copies."""
+        lens: dict[str, int] = {}
+        for ck in chunks:
+            with self._stage_lock:
+                staged = PEER_KV_STAGING.get((ck, layer_name))
+                if staged is not None:
+                    lens[ck] = int(staged[0].shape[0])
+                    continue
+                src = self._source(ck, device)
+                _, _, t, hkv, d = src.shape
                 if device.type == "cuda":
-                    ev = torch.cuda.Event()
-                    ev.record(self._side_stream)
-                    st.cuda_events[layer_name] = ev
-                st.events[layer_name].set()
-            total = sum(lens.values())
-            if total != st.expected_total:
-                raise RuntimeError(f"HcpRingKvConnector: staged prefix length {total} != expected "
-                                   f"external prefix {st.expected_total} (chunks={st.chunks})")
-        except BaseException as e:  # noqa: BLE001 - re-raised on the worker thread
-            st.error = e
-            for ev in st.events.values():
-                ev.set()
+                    with torch.cuda.stream(self._side_stream):
+                        k = torch.empty(t, hkv, d, dtype=src.dtype, device=device)
+                        v = torch.empty_like(k)
+                        src.copy_layer(layer_index(layer_name), k, v, self._side_stream)
+                else:
+                    k = torch.empty(t, hkv, d, dtype=src.dtype, device=device)
+                    v = torch.empty_like(k)
+                    src.copy_layer(layer_index(layer_name), k, v, None)
+                stage_peer_kv(ck, layer_name, k, v)
+                lens[ck] = t
+        done = None
+        if device.type == "cuda":
+            done = torch.cuda.Event()
+            done.record(self._side_stream)
+        return lens, done
 
     def start_load_kv(self, forward_context: "ForwardContext", **kwargs: Any) -> None:
         metadata = self._get_connector_metadata()
@@ -535,39 +487,32 @@ class HcpRingKvConnector(KVConnectorBase_V1):
             expected = align_down(req.prefix_len or self._prefix_len, self._block_size)
             if self._decode_owner:
                 self._register_decode(req, expected, device)   # may fail: before any other state
-            map_request_peer(req.first_block_id, req.chunk_keys)
-            self._live[req.req_id] = (req.first_block_id, list(req.chunk_keys))
-            for ck in req.chunk_keys:
-                self._chunk_refs[ck] = self._chunk_refs.get(ck, 0) + 1
-            st = _PrefillStream(req.req_id, layer_order, list(req.chunk_keys), expected)
-            self._streams[req.req_id] = st
-            st.thread = threading.Thread(target=self._stream_worker, args=(st, device), daemon=True)
-            st.thread.start()
+            self._ledger.hold(req.req_id, req.first_block_id, req.chunk_keys)
+            feed = LayerFeed(req.req_id, layer_order, list(req.chunk_keys), expected, stream_window())
+            self._feeds[req.req_id] = feed
+            chunks = list(req.chunk_keys)
+            feed.start(lambda ln, chunks=chunks: self._stage_layer(chunks, ln, device),
+                       init=(lambda: torch.cuda.set_device(device)) if device.type == "cuda" else None)
 
     def wait_for_layer_load(self, layer_name: str) -> None:
-        if not self._streams:
+        if not self._feeds:
             return
         idx = layer_index(layer_name)
         cur = torch.cuda.current_stream() if torch.cuda.is_available() else None
-        for st in list(self._streams.values()):
-            ev = st.events.get(layer_name)
-            if ev is None:
+        for feed in list(self._feeds.values()):
+            if not feed.covers(layer_name):
                 continue
-            ev.wait()
-            if st.error is not None:
-                raise RuntimeError(f"HcpRingKvConnector: prefill stream for req {st.req_id} failed") \
-                    from st.error
-            cev = st.cuda_events.get(layer_name)
+            cev = feed.wait(layer_name)
             if cev is not None and cur is not None:
                 cur.wait_event(cev)
-                for ck in st.chunks:
+                for ck in feed.chunks:
                     kv = PEER_KV_STAGING.get((ck, layer_name))
                     if kv is not None:
                         # read on the compute stream: keep the allocator from
                         # recycling these blocks before that work completes
                         kv[0].record_stream(cur)
                         kv[1].record_stream(cur)
-            st.consumed_idx = max(st.consumed_idx, idx)
+            feed.consumed(idx)
         if not self._drop_consumed:
             return
         # transient staging of layers already consumed goes away
@@ -636,44 +581,33 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         """Backend callback at a decode-ring request's first decode step:
         free its staged prefix (refcounted) and keep its ring registration
         for the decode phase (``ring_connector.py:978-987``)."""
-        req_id = next((rid for rid, (fb, _) in self._live.items() if fb == first_block_id), None)
+        req_id = self._ledger.request_of_block(first_block_id)
         if req_id is not None:
-            self._release_live_entry(req_id, clear_ring=False)
+            self._end_request(req_id, keep_ring_slot=True)
 
-    def _release_live_entry(self, req_id: str, clear_ring: bool = True) -> None:
-        st = self._streams.pop(req_id, None)
-        if st is not None:
-            st.done.set()
-            if st.thread is not None:
-                st.thread.join()
-        if clear_ring and req_id in self._decode_slot_of:
-            slot, fb = self._decode_slot_of.pop(req_id)
-            clear_decode_ring(fb)
-            self._decode_free_slots.append(slot)
-        live = self._live.pop(req_id, None)
-        if live is None:
-            return
-        first_block_id, chunk_keys = live
-        unmap_request_peer(first_block_id)
-        for ck in chunk_keys:
-            refs = self._chunk_refs.get(ck, 0) - 1
-            if refs <= 0:
-                self._chunk_refs.pop(ck, None)
-                drop_chunk_kv(ck)
-            else:
-                self._chunk_refs[ck] = refs
+    def _end_request(self, req_id: str, keep_ring_slot: bool = False) -> None:
+        """Stop the request's staging thread, release its chunk holds and,
+        unless kept for its decode phase, its decode-ring slot."""
+        feed = self._feeds.pop(req_id, None)
+        if feed is not None:
+            feed.stop()
+        if not keep_ring_slot:
+            fb = self._slots.give_back(req_id)
+            if fb is not None:
+                clear_decode_ring(fb)
+        self._ledger.release(req_id)
 
     def _cleanup_finished(self, finished_req_ids) -> None:
         for req_id in finished_req_ids:
-            self._release_live_entry(req_id)
+            self._end_request(req_id)
 
     @classmethod
     def get_required_kvcache_layout(cls, vllm_config: "VllmConfig") -> str | None:
         return None
 
     def shutdown(self) -> None:
-        for req_id in list(self._live) + list(self._decode_slot_of):
-            self._release_live_entry(req_id)
+        for req_id in self._ledger.requests() + self._slots.holders():
+            self._end_request(req_id)
         from . import ring_backend
         if ring_backend._STAGING_RELEASE_FN == self._release_request_staging:
             set_staging_release_fn(None)
@@ -682,9 +616,7 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         self._decode_stop.set()
         if self._decode_thread is not None:
             self._decode_thread.join(timeout=30)
-        for ck in list(self._chunk_refs):
-            drop_chunk_kv(ck)
-        self._chunk_refs.clear()
+        self._ledger.release_all()
         for src in self._sources.values():
             close = getattr(src, "close", None)
             if close is not None:

@@ -91,7 +91,7 @@ def test_poll_backoff():
         open(os.path.join(shared, "run", "c0", "_READY"), "w").close()
         # inside the back-off window the marker is not looked at again
         assert conn.get_num_new_matched_tokens(req, 0) == (None, True)
-        conn._ready_next_poll.clear()
+        conn._readiness.look_again_now()
         assert conn.get_num_new_matched_tokens(req, 0) == (64, False)
 
 
@@ -214,14 +214,14 @@ def test_streaming_window_and_refcounts(tmp_path, monkeypatch, window):
     # is shared with r1) and its ring registration stays (ring_connector.py:978-987)
     rb._release_staged_for_request(3)
     assert 3 not in rb.PEER_REQ_MAP and 9 in rb.PEER_REQ_MAP and 3 in rb.DECODE_RING_MAP
-    assert not any(key[0] == "c1" for key in rb.PEER_KV_STAGING) and conn._chunk_refs == {"c0": 1}
+    assert not any(key[0] == "c1" for key in rb.PEER_KV_STAGING) and conn._ledger.holder_counts() == {"c0": 1}
     # r0 finishes: its ring slot is released, c0 (shared with r1) stays
     conn.bind_connector_metadata(_load_meta([], finished=["r0"]))
     conn.start_load_kv(fk.forward_context({}))
     assert 3 not in rb.PEER_REQ_MAP and 9 in rb.PEER_REQ_MAP
     assert not any(key[0] == "c1" for key in rb.PEER_KV_STAGING)
     assert any(key[0] == "c0" for key in rb.PEER_KV_STAGING)
-    assert list(rb.DECODE_RING_MAP) == [9] and conn._decode_free_slots == [2, 3, 0]
+    assert list(rb.DECODE_RING_MAP) == [9] and list(conn._slots.free) == [2, 3, 0]
     conn.get_finished({"r1"})
     assert rb.PEER_REQ_MAP == {} and rb.PEER_KV_STAGING == {} and rb.DECODE_RING_MAP == {}
     conn.shutdown()
@@ -323,7 +323,7 @@ def test_prefix_length_mismatch_raises(tmp_path):
     conn.bind_connector_metadata(_load_meta([("r0", 1, ["c0"], 48)]))   # 48 expected, 32 staged
     names = _layers(2)
     conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in names}))
-    conn._streams["r0"].thread.join()
+    conn._feeds["r0"].join()
     with pytest.raises(RuntimeError):
         conn.wait_for_layer_load(names[1])
     conn.shutdown()
@@ -521,5 +521,5 @@ def test_decode_ring_slots_exhausted(tmp_path):
     conn.bind_connector_metadata(_load_meta([("r0", 1, ["c0"], 16), ("r1", 2, ["c0"], 16)]))
     with pytest.raises(RuntimeError, match="slots"):
         conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in _layers(2)}))
-    assert list(conn._live) == ["r0"] and 2 not in rb.PEER_REQ_MAP   # r1 left no state behind
+    assert conn._ledger.requests() == ["r0"] and 2 not in rb.PEER_REQ_MAP   # r1 left no state behind
     conn.shutdown()
