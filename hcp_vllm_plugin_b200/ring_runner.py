@@ -201,11 +201,20 @@ class RingPrefill:
         qsrc = self.q_comb if g else q
         first = True
         used = [False] * len(self.slot_k)
+        launched: list[tuple[int, torch.cuda.Event]] = []   # (hop, end of its launch) on s_hop
         for hop in self.hops:
             s = hop.slot
             with self._on(s_comm):
-                if s >= 0 and used[s] and self._cuda:
-                    s_comm.wait_event(self.slot_free[s])
+                if self._cuda:
+                    # A posted NCCL kernel holds SMs while it waits for its
+                    # peer.  The peer's receive slot frees when its launch two
+                    # hops back ends; this rank's own launch from then is the
+                    # local stand-in, so hop h is posted only after it.
+                    gate = [ev for hh, ev in launched if hh <= hop.hop - 2]
+                    if gate:
+                        s_comm.wait_event(gate[-1])
+                    if s >= 0 and used[s]:
+                        s_comm.wait_event(self.slot_free[s])
                 hop_ops = []
                 if hop.send_to is not None:
                     dst = self._peer(hop.send_to)
@@ -237,6 +246,7 @@ class RingPrefill:
                            k_b=k, v_b=v, **merge)
                 if self._cuda:
                     self.slot_free[s].record(s_hop)
+                    launched.append((hop.hop, self._record(s_hop)))
             used[s] = True
             first = False
         if g and first:
@@ -258,6 +268,11 @@ class RingPrefill:
                                          dist.P2POp(dist.isend, self.lse_help, dst, group=grp)])
         if give:
             with self._on(s_comm):
+                if self._cuda:
+                    # the helper sends when its launches end: posting the
+                    # receive before this rank's own hop launches end would
+                    # hold SMs for the whole layer
+                    s_comm.wait_stream(s_hop)
                 src = self._peer(self.helper)
                 ret_works = self._p2p([dist.P2POp(dist.irecv, self.o_part, src, group=grp),
                                        dist.P2POp(dist.irecv, self.lse_part, src, group=grp)])
