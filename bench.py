@@ -222,7 +222,8 @@ def config(args):
             "layers": args.layers, "heads": H, "kv_heads": HKV, "head_dim": D,
             "chunk_per_gpu": args.seq // max(1, args.gpus), "parallelism": f"cp{args.gpus}",
             "global_batch": 1, "l2": "inputs larger than L2 (q 0.94 GB/layer at N=1)",
-            "schedule": "balanced pairs" if not args.no_balance else "plain ring"}
+            "schedule": "balanced pairs" if not args.no_balance else "plain ring",
+            "transport": args.ring_transport if args.gpus > 1 else "none"}
 
 
 def main():
@@ -238,6 +239,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-balance", action="store_true")
     ap.add_argument("--no-side", action="store_true")
+    ap.add_argument("--ring-transport", choices=["ce", "p2p"], default="ce",
+                    help="how chunks move between ranks: copy-engine pulls (default) or NCCL send/recv")
     ap.add_argument("--kernel", choices=["fwd", "decode"], default=None,
                     help="profiling mode: time one kernel on a small case and exit")
     ap.add_argument("--decode-seqs", type=int, default=16)
@@ -290,7 +293,8 @@ def main():
     seq, L = args.seq, args.layers
     chunk = seq // world
     scale = D ** -0.5
-    runner = RingPrefill(seq, H, HKV, D, scale, dev, balance=not args.no_balance)
+    runner = RingPrefill(seq, H, HKV, D, scale, dev, balance=not args.no_balance,
+                         transport=args.ring_transport if world > 1 else None)
 
     # resident per-layer inputs of this rank's chunk (seeded)
     qs, ks, vs = [], [], []

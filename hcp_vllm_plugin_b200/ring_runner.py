@@ -12,12 +12,9 @@ Per layer on rank x (chunk C, ``give`` rows handed to a helper, P ranks):
 
 * caller's stream (lowest priority), at once:
     own rows [0, C) vs the own chunk, causal  ->  acc_own (fp32 O, LSE)
-* communication (NCCL send/recv on its own stream), per hop h = 1..P-1:
-    send the own chunk's K/V to rank x+h if that rank reads chunk x, and
-    receive chunk x-h into one of two slots if this rank reads it; a slot is
-    refilled only after the launch that read it has finished.  Each hop is a
-    permutation of the ranks, so no link carries two chunks at once.  Before
-    the hops the owner sends Q rows [0, give) to its helper.
+* communication stream, hop by hop h = 1..P-1: chunk x-h is brought into
+  one of two receive slots if this rank reads it; a slot is refilled only
+  after the launch that read it has finished.
 * hop stream (high priority), one launch per received chunk, each merging
   into the previous one's (O, LSE) in its epilogue (acc_peer):
     own rows [give, C) vs the chunk when it precedes x, and the rows computed
@@ -29,13 +26,29 @@ Per layer on rank x (chunk C, ``give`` rows handed to a helper, P ranks):
   stream merges acc_own with acc_peer for rows [give, C) and acc_own with the
   returned partial for rows [0, give), writing the output dtype directly.
 
-TMA reads only this GPU's HBM: received chunks sit in local slots.  Every rank
-issues its collectives in the same order (Q rows, hops 1..P-1, partials).
+Transports (``transport=``):
+
+* ``"ce"`` (default on CUDA): every rank copies its K/V (and the Q rows its
+  helper computes) into an outbox buffer exported once by CUDA IPC; after one
+  4-byte all-reduce per layer (every outbox filled) each receiver pulls the
+  chunks it reads from the owners' outboxes with the copy engine, when its
+  slot is free.  No SM waits on a peer: a NCCL kernel posted before its peer
+  is ready holds SMs until the peer arrives, which on 8 ranks cost more than
+  the transfers.  Outboxes alternate between two buffers by layer parity; a
+  rank refills one only after the next layer's all-reduce, which every rank
+  reaches after its pulls of the layer before.
+* ``"p2p"``: NCCL send/recv per hop (the only transport of a CPU / gloo
+  group, where the tests of the schedule run).
+
+The partials go back by NCCL send/recv; the owner posts its receive once its
+own hop launches end.  TMA reads only this GPU's HBM: received chunks sit in
+local slots.  Every rank issues its collectives in the same order.
 """
 
 from __future__ import annotations
 
 import contextlib
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -61,7 +74,7 @@ class RingPrefill:
 
     def __init__(self, seq_len: int, num_heads: int, num_kv_heads: int, head_dim: int,
                  scale: float, device: torch.device, dtype: torch.dtype = torch.bfloat16,
-                 group=None, balance: bool = True, slots: int = 2):
+                 group=None, balance: bool = True, slots: int = 2, transport: str | None = None):
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.world = dist.get_world_size(group)
@@ -113,17 +126,75 @@ class RingPrefill:
             self.o_part = torch.empty(self.give, num_heads, head_dim, dtype=f32, device=device)
             self.lse_part = torch.empty(num_heads, self.give, dtype=f32, device=device)
         self._cuda = device.type == "cuda"
+        if transport is None:
+            transport = "ce" if self._cuda else "p2p"
+        if transport not in ("ce", "p2p") or (transport == "ce" and not self._cuda):
+            raise ValueError(f"ring prefill: transport {transport!r} (ce needs CUDA tensors; p2p works on both)")
+        self.transport = transport if self.world > 1 else "none"
         if self._cuda and self.world > 1:
             self.s_hop = torch.cuda.Stream(device, priority=-100)   # clamped to the highest
             self.s_comm = torch.cuda.Stream(device, priority=-100)
             self.slot_free = [torch.cuda.Event() for _ in self.slot_k]
         # device-side failures of earlier layers surface as HcpError at the next
         self._watch = C.DeviceStatusWatch() if self._cuda else None
+        self._peer_bases: list[int] = []
         if self.world > 1:
             # NCCL wants every rank of a group in its first collective; the
             # per-hop send/recv calls involve only pairs
             dist.barrier(group=group)
+        if self.transport == "ce":
+            self._open_outboxes()
         self.launches = 0  # kernels of this library launched (for the bench's count)
+
+    # ------------------------------------------------------------------ ce transport
+    def _box_offsets(self, rank: int, parity: int) -> tuple[int, int, int]:
+        """Element offsets of K, V and the handed-off Q rows in parity half
+        ``parity`` of ``rank``'s outbox (its halves hold its own ``give``)."""
+        kv = self.chunk * self.Hkv * self.D
+        base = parity * (2 * kv + self.plan.rows_given(rank) * self.H * self.D)
+        return base, base + kv, base + 2 * kv
+
+    def _open_outboxes(self) -> None:
+        """Allocate this rank's outbox (two parity halves of [K | V | Q rows
+        [0, give)]), export it, and map the outboxes of the ranks whose chunk
+        or Q rows this rank reads."""
+        c, hkv, h, d = self.chunk, self.Hkv, self.H, self.D
+        self.outbox = torch.empty(2, 2 * c * hkv * d + self.give * h * d, dtype=self.dtype, device=self.device)
+        handle = (ctypes.c_uint8 * 64)()
+        offset = ctypes.c_int64()
+        lib = C.load()
+        C.check(lib.hcp_ipc_export(self.outbox.data_ptr(), handle, ctypes.byref(offset)), "hcp_ipc_export")
+        mine = (bytes(handle).hex(), int(offset.value))
+        allx: list = [None] * self.world
+        dist.all_gather_object(allx, mine, group=self.group)
+        need = {hp.recv_chunk for hp in self.hops if hp.recv_chunk is not None}
+        if self.owner_give:
+            need.add(self.owner)
+        self._elt = self.outbox.element_size()
+        self._peer_box: dict[int, int] = {}
+        dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        for r in sorted(need):
+            hx, off = allx[r]
+            base = ctypes.c_void_p()
+            C.check(lib.hcp_ipc_open(bytes.fromhex(hx), dev, ctypes.byref(base)), "hcp_ipc_open")
+            self._peer_bases.append(base.value)
+            self._peer_box[r] = base.value + off
+        self._sig = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._parity = 0
+
+    def _pull(self, dst: torch.Tensor, rank: int, elem_off: int, stream) -> None:
+        """Copy engine: ``dst.numel()`` elements of ``rank``'s outbox from
+        element ``elem_off`` into ``dst`` (stream-ordered)."""
+        src = self._peer_box[rank] + elem_off * self._elt
+        C.check(C.load().hcp_peer_copy(dst.data_ptr(), src, dst.numel() * self._elt, stream.cuda_stream),
+                "hcp_peer_copy")
+
+    def close(self) -> None:
+        """Unmap the peers' outboxes (the buffers stay with their owners)."""
+        lib = C.load() if self._peer_bases else None
+        for b in self._peer_bases:
+            lib.hcp_ipc_close(b)
+        self._peer_bases = []
 
     # ------------------------------------------------------------------ helpers
     def _attn(self, q, items, out, lse, **src):
@@ -174,6 +245,7 @@ class RingPrefill:
             raise ValueError("ring prefill: q, k and v must be contiguous (they are sent as they are)")
         grp = self.group
         give, g = self.give, self.owner_give
+        ce = self.transport == "ce"
         s0 = torch.cuda.current_stream(self.device) if self._cuda else None
         s_hop = self.s_hop if self._cuda else None
         s_comm = self.s_comm if self._cuda else None
@@ -186,45 +258,65 @@ class RingPrefill:
         if self._cuda:
             s_comm.wait_event(ev_in)
             s_hop.wait_event(ev_in)
-        with self._on(s_comm):
-            q_ops = []
-            if give:
-                q_ops.append(dist.P2POp(dist.isend, q[:give], self._peer(self.helper), group=grp))
+        send_works: list = []
+        par = 0
+        if ce:
+            par = self._parity
+            self._parity ^= 1
+            k_off, v_off, q_off = self._box_offsets(x, par)
+            with self._on(s_comm):
+                box = self.outbox.view(-1)
+                kv = c * self.Hkv * self.D
+                box[k_off:k_off + kv].view_as(k).copy_(k)
+                box[v_off:v_off + kv].view_as(v).copy_(v)
+                if give:
+                    box[q_off:q_off + give * self.H * self.D].view(give, self.H, self.D).copy_(q[:give])
+                # every outbox of this layer is filled (and, in each rank's
+                # stream order, its pulls of the layer before are done)
+                dist.all_reduce(self._sig, op=dist.ReduceOp.MAX, group=grp, async_op=True).wait()
+                if g:
+                    self._pull(self.q_comb[c:], self.owner, self._box_offsets(self.owner, par)[2], s_comm)
+            ev_q = self._record(s_comm) if g else None
+        else:
+            with self._on(s_comm):
+                q_ops = []
+                if give:
+                    q_ops.append(dist.P2POp(dist.isend, q[:give], self._peer(self.helper), group=grp))
+                if g:
+                    q_ops.append(dist.P2POp(dist.irecv, self.q_comb[c:], self._peer(self.owner), group=grp))
+                q_works = self._p2p(q_ops)
             if g:
-                q_ops.append(dist.P2POp(dist.irecv, self.q_comb[c:], self._peer(self.owner), group=grp))
-            q_works = self._p2p(q_ops)
-        if g:
-            with self._on(s_hop):
-                for w in q_works:
-                    w.wait()
-        send_works = list(q_works) if give else []
+                with self._on(s_hop):
+                    for w in q_works:
+                        w.wait()
+            send_works = list(q_works) if give else []
         qsrc = self.q_comb if g else q
         first = True
         used = [False] * len(self.slot_k)
-        launched: list[tuple[int, torch.cuda.Event]] = []   # (hop, end of its launch) on s_hop
         for hop in self.hops:
             s = hop.slot
+            if ce and hop.recv_chunk is None:
+                continue          # the receivers pull: nothing to do for a send
             with self._on(s_comm):
-                if self._cuda:
-                    # A posted NCCL kernel holds SMs while it waits for its
-                    # peer.  The peer's receive slot frees when its launch two
-                    # hops back ends; this rank's own launch from then is the
-                    # local stand-in, so hop h is posted only after it.
-                    gate = [ev for hh, ev in launched if hh <= hop.hop - 2]
-                    if gate:
-                        s_comm.wait_event(gate[-1])
-                    if s >= 0 and used[s]:
-                        s_comm.wait_event(self.slot_free[s])
-                hop_ops = []
-                if hop.send_to is not None:
-                    dst = self._peer(hop.send_to)
-                    hop_ops += [dist.P2POp(dist.isend, k, dst, group=grp),
-                                dist.P2POp(dist.isend, v, dst, group=grp)]
-                if hop.recv_chunk is not None:
-                    src = self._peer(hop.recv_chunk)
-                    hop_ops += [dist.P2POp(dist.irecv, self.slot_k[s], src, group=grp),
-                                dist.P2POp(dist.irecv, self.slot_v[s], src, group=grp)]
-                works = self._p2p(hop_ops)
+                if s >= 0 and used[s] and self._cuda:
+                    s_comm.wait_event(self.slot_free[s])
+                works = []
+                if ce:
+                    pk, pv, _ = self._box_offsets(hop.recv_chunk, par)
+                    self._pull(self.slot_k[s], hop.recv_chunk, pk, s_comm)
+                    self._pull(self.slot_v[s], hop.recv_chunk, pv, s_comm)
+                    ev_chunk = self._record(s_comm)
+                else:
+                    hop_ops = []
+                    if hop.send_to is not None:
+                        dst = self._peer(hop.send_to)
+                        hop_ops += [dist.P2POp(dist.isend, k, dst, group=grp),
+                                    dist.P2POp(dist.isend, v, dst, group=grp)]
+                    if hop.recv_chunk is not None:
+                        src = self._peer(hop.recv_chunk)
+                        hop_ops += [dist.P2POp(dist.irecv, self.slot_k[s], src, group=grp),
+                                    dist.P2POp(dist.irecv, self.slot_v[s], src, group=grp)]
+                    works = self._p2p(hop_ops)
             if hop.recv_chunk is None:
                 # only sends: waited for at the end.  A hop that also receives
                 # is waited for on the hop stream below, which the caller's
@@ -233,6 +325,8 @@ class RingPrefill:
                 send_works += works
                 continue
             with self._on(s_hop):
+                if ce:
+                    s_hop.wait_event(ev_chunk)     # after the Q rows' pull too (stream order)
                 for w in works:
                     w.wait()
                 items = []
@@ -246,15 +340,17 @@ class RingPrefill:
                            k_b=k, v_b=v, **merge)
                 if self._cuda:
                     self.slot_free[s].record(s_hop)
-                    launched.append((hop.hop, self._record(s_hop)))
             used[s] = True
             first = False
         if g and first:
             # a helper that receives nothing: the partner's rows see only this chunk
             with self._on(s_hop):
+                if ce:
+                    s_hop.wait_event(ev_q)
                 self._attn(qsrc, [(c, g, 0, c, (A, 0, c, -1), None)], self.acc_peer, self.lse_peer,
                            k_a=k, v_a=v)
-        # 3. partials back to the owners
+        # 3. partials back to the owners (NCCL; a posted NCCL kernel holds SMs
+        # until its peer arrives, so each side posts once its own launches end)
         ret_works = []
         if g:
             with self._on(s_hop):
@@ -269,9 +365,6 @@ class RingPrefill:
         if give:
             with self._on(s_comm):
                 if self._cuda:
-                    # the helper sends when its launches end: posting the
-                    # receive before this rank's own hop launches end would
-                    # hold SMs for the whole layer
                     s_comm.wait_stream(s_hop)
                 src = self._peer(self.helper)
                 ret_works = self._p2p([dist.P2POp(dist.irecv, self.o_part, src, group=grp),
@@ -295,8 +388,11 @@ class RingPrefill:
             self._merge(out[:give], self.acc_own[:give], self.lse_own[:, :give], self.o_part, self.lse_part,
                         o_lse)
         # the caller may overwrite q/k/v once this returns: wait for the sends
+        # (and, with ce, for the outbox copies on the communication stream)
         for w in send_works:
             w.wait()
+        if self._cuda:
+            s0.wait_stream(s_comm)
         if self._watch is not None:
             self._watch.record(s0)
         return out

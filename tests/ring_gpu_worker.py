@@ -1,10 +1,14 @@
 """Worker for test_ring_multi_gpu.py (run under torchrun, one rank per GPU).
 
 Each rank runs RingPrefill.forward on its contiguous chunk of a seeded
-sequence over NCCL; rank 0 gathers the chunks and compares them with the
+sequence, once per transport (copy-engine pulls from exported outboxes, and
+NCCL send/recv); rank 0 gathers the chunks and compares them with the
 single-GPU fused kernel over the whole sequence and with the CPU oracle on
-sampled rows (the bar of tests/parity.py).  Prints one JSON line on rank 0
-and exits non-zero on mismatch.
+sampled rows (the bar of tests/parity.py).  Three layers run back to back
+with V scaled by 3, 2 and 1, so a chunk pulled from an outbox a layer too
+early or too late (the outboxes alternate by layer parity) shows up in the
+last layer's output.  Prints one JSON line per transport on rank 0 and exits
+non-zero on mismatch.
 """
 
 import datetime
@@ -38,47 +42,56 @@ def main():
     q = torch.randn(seq, H, D, generator=g).bfloat16()
     k = torch.randn(seq, HKV, D, generator=g).bfloat16()
     v = torch.randn(seq, HKV, D, generator=g).bfloat16()
-    runner = RingPrefill(seq, H, HKV, D, D ** -0.5, dev)
-    c = runner.chunk
-    sl = slice(rank * c, (rank + 1) * c)
-    out = torch.empty(c, H, D, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(H, c, dtype=torch.float32, device=dev)
-    for _ in range(2):  # twice: buffers are reused across layers
-        runner.forward(q[sl].to(dev), k[sl].to(dev), v[sl].to(dev), out, lse)
-    outs = [torch.empty_like(out) for _ in range(world)]
-    dist.all_gather(outs, out)
-    lses = [torch.empty_like(lse) for _ in range(world)]
-    dist.all_gather(lses, lse)
     ok = True
-    if rank == 0:
-        full_o, full_lse = ops.ring_attn_with_lse(q.to(dev), k.to(dev), v.to(dev), D ** -0.5, 0)
-        got = torch.cat(outs).float().cpu().numpy()
-        got_lse = torch.cat(lses, 1).cpu().numpy()
-        single = full_o.float().cpu().numpy()
-        # against the one-GPU launch over the whole sequence: equal or one bf16 step apart
-        step = P.step_of(single, torch.bfloat16)
-        d = np.abs(got - single)
-        steps_ok = bool((d <= np.maximum(2e-3, step * 1.0001)).all())
-        # against the oracle, on sampled rows (chunk edges included): the parity bar
-        rows = np.unique(np.r_[np.linspace(0, seq - 1, 24).astype(int), [c - 1, c, seq - 1]])
-        qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
-        want = np.empty((len(rows), H, D), np.float32)
-        want_lse = np.empty((H, len(rows)), np.float32)
-        for i, r in enumerate(rows):
-            o, l = ro.attn_with_lse(qf[r:r + 1], kf[: r + 1], vf[: r + 1], D ** -0.5, int(r))
-            want[i], want_lse[:, i] = o[0], l[:, 0]
-        try:
-            st = P.check_out(got[rows], want, f"ring N={world} sampled rows")
-            P.check_lse(got_lse[:, rows], want_lse, f"ring N={world}")
-            oracle_ok, line = True, st.line()
-        except AssertionError as e:
-            oracle_ok, line = False, str(e)
-        res = {"world": world, "seq": seq, "give": runner.plan.give,
-               "max_vs_single_gpu": float(d.max()), "within_one_step_of_single_gpu": steps_ok,
-               "lse_max_vs_single_gpu": float(np.abs(got_lse - full_lse.cpu().numpy()).max()),
-               "oracle": line, "device_status": _capi.device_status()}
-        ok = steps_ok and oracle_ok and res["lse_max_vs_single_gpu"] <= 1e-3 and res["device_status"] == 0
-        print(json.dumps(res), flush=True)
+    full = None
+    for transport in ("ce", "p2p"):
+        runner = RingPrefill(seq, H, HKV, D, D ** -0.5, dev, transport=transport)
+        c = runner.chunk
+        sl = slice(rank * c, (rank + 1) * c)
+        out = torch.empty(c, H, D, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(H, c, dtype=torch.float32, device=dev)
+        qd, kd, vd = q[sl].to(dev), k[sl].to(dev), v[sl].to(dev)
+        layers = [(qd, kd, (vd.float() * sc).bfloat16()) for sc in (3.0, 2.0)] + [(qd, kd, vd)]
+        for ql, kl, vl in layers:  # buffers and outboxes are reused across layers
+            runner.forward(ql, kl, vl, out, lse)
+        torch.cuda.synchronize()
+        runner.close()
+        outs = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(outs, out)
+        lses = [torch.empty_like(lse) for _ in range(world)]
+        dist.all_gather(lses, lse)
+        if rank == 0:
+            if full is None:
+                full = ops.ring_attn_with_lse(q.to(dev), k.to(dev), v.to(dev), D ** -0.5, 0)
+            full_o, full_lse = full
+            got = torch.cat(outs).float().cpu().numpy()
+            got_lse = torch.cat(lses, 1).cpu().numpy()
+            single = full_o.float().cpu().numpy()
+            # against the one-GPU launch over the whole sequence: equal or one bf16 step apart
+            step = P.step_of(single, torch.bfloat16)
+            d = np.abs(got - single)
+            steps_ok = bool((d <= np.maximum(2e-3, step * 1.0001)).all())
+            # against the oracle, on sampled rows (chunk edges included): the parity bar
+            rows = np.unique(np.r_[np.linspace(0, seq - 1, 24).astype(int), [c - 1, c, seq - 1]])
+            qf, kf, vf = q.float().numpy(), k.float().numpy(), v.float().numpy()
+            want = np.empty((len(rows), H, D), np.float32)
+            want_lse = np.empty((H, len(rows)), np.float32)
+            for i, r in enumerate(rows):
+                o, l = ro.attn_with_lse(qf[r:r + 1], kf[: r + 1], vf[: r + 1], D ** -0.5, int(r))
+                want[i], want_lse[:, i] = o[0], l[:, 0]
+            try:
+                st = P.check_out(got[rows], want, f"ring N={world} {transport} sampled rows")
+                P.check_lse(got_lse[:, rows], want_lse, f"ring N={world} {transport}")
+                oracle_ok, line = True, st.line()
+            except AssertionError as e:
+                oracle_ok, line = False, str(e)
+            res = {"world": world, "seq": seq, "transport": transport, "give": runner.plan.give,
+                   "max_vs_single_gpu": float(d.max()), "within_one_step_of_single_gpu": steps_ok,
+                   "lse_max_vs_single_gpu": float(np.abs(got_lse - full_lse.cpu().numpy()).max()),
+                   "oracle": line, "device_status": _capi.device_status()}
+            ok = ok and steps_ok and oracle_ok and res["lse_max_vs_single_gpu"] <= 1e-3 \
+                and res["device_status"] == 0
+            print(json.dumps(res), flush=True)
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.broadcast(flag, 0)
     dist.barrier(device_ids=[local])

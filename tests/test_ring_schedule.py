@@ -55,3 +55,37 @@ def test_hop_schedule_pairs_and_coverage(world, balance):
     # moved bytes: only what is read, never more than an all-gather
     moved = sum(len([h for h in sched[x].values() if h.recv_chunk is not None]) for x in range(world))
     assert moved <= world * (world - 1)
+
+
+def test_outbox_pulls_stay_inside_the_owners_outbox():
+    """Every copy-engine pull of the ce transport (K, V of a received chunk;
+    the partner's Q rows) reads inside the source rank's outbox, for both
+    parity halves, and the halves do not overlap."""
+    from types import SimpleNamespace
+
+    from hcp_vllm_plugin_b200.ring_runner import RingPrefill
+    from hcp_vllm_plugin_b200.ring_schedule import hop_schedule
+
+    H, HKV, D = 28, 4, 128
+    for world in (2, 3, 4, 5, 6, 8):
+        chunk = 2048
+        plan = plan_balanced(world, chunk)
+        kv = chunk * HKV * D
+        size = {r: 2 * (2 * kv + plan.rows_given(r) * H * D) for r in range(world)}
+        for x in range(world):
+            me = SimpleNamespace(chunk=chunk, Hkv=HKV, H=H, D=D, plan=plan)
+            pulls = [(hp.recv_chunk, "k") for hp in hop_schedule(plan, x) if hp.recv_chunk is not None]
+            pulls += [(hp.recv_chunk, "v") for hp in hop_schedule(plan, x) if hp.recv_chunk is not None]
+            owner = plan.helped_owner(x)
+            if owner is not None and plan.rows_given(owner):
+                pulls.append((owner, "q"))
+            for r, what in pulls:
+                for par in (0, 1):
+                    k_off, v_off, q_off = RingPrefill._box_offsets(me, r, par)
+                    off, n = {"k": (k_off, kv), "v": (v_off, kv),
+                              "q": (q_off, plan.rows_given(r) * H * D)}[what]
+                    assert 0 <= off and off + n <= size[r], (world, x, r, what, par)
+                    assert n > 0
+                    # parity halves are disjoint
+                    half = size[r] // 2
+                    assert (off >= half) == (par == 1) and (off + n <= half) == (par == 0)
