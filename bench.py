@@ -659,12 +659,13 @@ def fwd_issuer_variants(seq: int) -> dict:
     named-barrier issuer, 2 variant 1 with a quarter of the exponentials on
     the FMA pipe, 3-5 the mbarrier issuer on 384 threads with setmaxnreg
     register split and packed f32x2 softmax math, with 1/4, 3/8 and none of
-    the exponentials on the FMA pipe.  Each runs in a fresh process, since the
+    the exponentials on the FMA pipe, 6 the named-barrier issuer on 384 threads
+    with the setmaxnreg split.  Each runs in a fresh process, since the
     library reads the switch once per process.  Reported beside the headline
     only."""
     out = {}
     names = ("mbarrier_issuer", "named_barrier_issuer", "named_barrier_poly_exp2",
-             "wide_poly_quarter", "wide_poly_three_eighths", "wide_no_poly")
+             "wide_poly_quarter", "wide_poly_three_eighths", "wide_no_poly", "named_barrier_wide")
     for variant, name in enumerate(names):
         env = dict(os.environ, HCP_FWD_VARIANT=str(variant))
         cmd = [sys.executable, os.path.abspath(__file__), "--kernel", "fwd", "--seq", str(seq), "--iters", "5"]

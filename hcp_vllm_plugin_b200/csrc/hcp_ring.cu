@@ -103,15 +103,16 @@ bool encode_rows_heads(CUtensorMap* m, bool f16, const void* base, int64_t rows,
 }
 
 std::mutex g_attr_mu;
-bool g_attr_done[2][2][7][64];  // variants 0-5, and 6 for the LIST kernel
+bool g_attr_done[2][2][8][64];  // variants 0-6, and 7 for the LIST kernel
 bool g_dec_attr_done[2][2][64];
 
-// Forward kernel variant (read once per process): HCP_FWD_VARIANT=0..5, or
+// Forward kernel variant (read once per process): HCP_FWD_VARIANT=0..6, or
 // HCP_FWD_NAMED_BARRIERS=1 (1) / HCP_FWD_POLY_EXP2=1 (2).  0 - the mbarrier
 // MMA issuer; 1 - the named-barrier issuer; 2 - 1 with a quarter of the
 // exponentials on the FMA pipe; 3, 4, 5 - the mbarrier issuer on 384 threads
 // with the registers split by setmaxnreg and packed f32x2 softmax math, with
-// a quarter, three eighths or none of the exponentials on the FMA pipe.
+// a quarter, three eighths or none of the exponentials on the FMA pipe; 6 -
+// the named-barrier issuer on 384 threads with the setmaxnreg split.
 int fwd_variant() {
   static const int v = [] {
     auto on = [](const char* name) {
@@ -119,7 +120,7 @@ int fwd_variant() {
       return e != nullptr && e[0] == '1';
     };
     const char* e = std::getenv("HCP_FWD_VARIANT");
-    if (e != nullptr && e[0] >= '0' && e[0] <= '5' && e[1] == 0) return e[0] - '0';
+    if (e != nullptr && e[0] >= '0' && e[0] <= '6' && e[1] == 0) return e[0] - '0';
     return on("HCP_FWD_POLY_EXP2") ? 2 : on("HCP_FWD_NAMED_BARRIERS") ? 1 : 0;
   }();
   return v;
@@ -132,7 +133,7 @@ int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
   {
     std::lock_guard<std::mutex> lk(g_attr_mu);
-    bool& done = g_attr_done[D == 128][F16][LIST ? 6 : V][dev];
+    bool& done = g_attr_done[D == 128][F16][LIST ? 7 : V][dev];
     if (!done) {
       if (cudaFuncSetAttribute(ring_fwd_kernel<D, F16, V, LIST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                smem) != cudaSuccess)
@@ -162,6 +163,7 @@ int launch_fwd(const FwdParams& p, int grid, cudaStream_t st, bool list) {
     case 3: return launch_fwd<D, F16, 3>(p, grid, st);
     case 4: return launch_fwd<D, F16, 4>(p, grid, st);
     case 5: return launch_fwd<D, F16, 5>(p, grid, st);
+    case 6: return launch_fwd<D, F16, 6>(p, grid, st);
     default: return launch_fwd<D, F16, 0>(p, grid, st);
   }
 }

@@ -43,7 +43,10 @@
 // Variants (template parameter V, chosen per process by the host): 0 - the
 // MMA issuer waits on mbarriers; 1 - it meets the softmax warpgroups at
 // named barriers only and they wait on the mbarriers instead; 2 - as 1, with
-// a quarter of the exponentials computed on the FMA pipe (exp2_poly).
+// a quarter of the exponentials computed on the FMA pipe (exp2_poly); 3-5 -
+// as 0 on 384 threads with the registers split by setmaxnreg and packed
+// softmax math (a quarter, three eighths, none of the exponentials on the
+// FMA pipe); 6 - as 1 on 384 threads with the setmaxnreg split.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -63,7 +66,7 @@ constexpr int kStages = 2;
 constexpr int kWarpTma = 8;
 constexpr int kWarpMma = 9;
 constexpr int kThreads = 320;
-// Variants 3-5: a third warpgroup (warps 8-11: TMA, MMA, two idle) so the
+// Variants 3-6: a third warpgroup (warps 8-11: TMA, MMA, two idle) so the
 // registers can be split by setmaxnreg - 224 for each softmax thread, 56 for
 // the producer warpgroup (2*128*224 + 128*56 = 384*168, the launch's total).
 constexpr int kThreadsWide = 384;
@@ -315,7 +318,7 @@ struct FwdSmem {
 template <int D, bool F16, int V = 0, bool LIST = false>
 __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
     ring_fwd_kernel(const __grid_constant__ FwdParams p) {
-  constexpr bool NB = V == 1 || V == 2;
+  constexpr bool NB = V == 1 || V == 2 || V == 6;
   constexpr bool kPoly = V == 2;
   constexpr bool kWide = V >= 3;
   static_assert(D == 64 || D == 128, "head_dim must be 64 or 128");
@@ -492,6 +495,28 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
                            wk.q_start + q0 + x * kBlockM);
     }
     int k_issued = 0, v_issued = 0;
+    const int bs = p.block_size;
+    const int nblk = kBlockN / bs;
+    // Block id of this lane's block of paged KV tile t (lanes < nblk), or an
+    // out-of-range id (TMA fills zeros) when the tile is not paged or the
+    // block lies outside the table.  Looked up one tile ahead, so the load's
+    // latency hides behind the waits and copies of the tile before.
+    auto lookup = [&](int t) {
+      int blk = static_cast<int>(p.num_blocks);
+      if (t < n_tiles && lane < nblk) {
+        const hcp_kv_segment sg = seg_at(tile_seg(t));
+        if (sg.src == HCP_SRC_PAGED) {
+          const int rel = tile_key0(t) + lane * bs;
+          const long long bidx = (static_cast<long long>(sg.start) + rel) / bs;
+          if (rel < sg.len && bidx < p.bt_stride && wk.paged_req >= 0 && wk.paged_req < p.bt_rows) {
+            const int v = __ldg(p.block_table + wk.paged_req * p.bt_stride + bidx);
+            if (v >= 0 && v < p.num_blocks) blk = v;
+          }
+        }
+      }
+      return blk;
+    };
+    int blk_next = lookup(0);
     for (int t = 0; t < n_tiles; ++t) {
       const int s = t % kStages;
       const uint32_t ph = (t / kStages) & 1;
@@ -501,20 +526,11 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
       const uint32_t s_v = s_k + kTileBytes;
       int blk_ids[8];
       const bool paged = seg.src == HCP_SRC_PAGED;
-      const int bs = p.block_size;
-      const int nblk = kBlockN / bs;
+      const int blk_cur = blk_next;
+      blk_next = lookup(t + 1);
       if (paged) {
-        int blk = static_cast<int>(p.num_blocks);  // out of range: TMA fills zeros
-        if (lane < nblk) {
-          const int rel = key0 + lane * bs;
-          const long long bidx = (static_cast<long long>(seg.start) + rel) / bs;
-          if (rel < seg.len && bidx < p.bt_stride && wk.paged_req >= 0 && wk.paged_req < p.bt_rows) {
-            const int v = __ldg(p.block_table + wk.paged_req * p.bt_stride + bidx);
-            if (v >= 0 && v < p.num_blocks) blk = v;
-          }
-        }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) blk_ids[i] = __shfl_sync(0xffffffffu, blk, i);
+        for (int i = 0; i < 8; ++i) blk_ids[i] = __shfl_sync(0xffffffffu, blk_cur, i);
       }
       if (!__all_sync(0xffffffffu, wait_bar(b_kempty(s), ph ^ 1, abort_flag, kErrWaitProducer)))
         break;

@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5"])
+@pytest.mark.parametrize("variant", ["1", "2", "3", "4", "5", "6"])
 def test_forward_variant_passes_the_forward_parity_suite(variant):
     env = dict(os.environ, HCP_FWD_VARIANT=variant)
     cmd = [sys.executable, "-m", "pytest", os.path.join(HERE, "test_fwd_gpu.py"), "-q", "-x", "-m", "gpu",
