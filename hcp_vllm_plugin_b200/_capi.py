@@ -85,6 +85,7 @@ class HcpFwdArgs(ctypes.Structure):
         ("ext", ctypes.POINTER(HcpKvSource)), ("num_ext", ctypes.c_int32), ("_pad5", ctypes.c_int32),
         ("seg_list", ctypes.POINTER(HcpKvSegment)), ("num_seg_list", ctypes.c_int32),
         ("_pad6", ctypes.c_int32),
+        ("window", ctypes.c_int32), ("_pad7", ctypes.c_int32),
     ]
 
 

@@ -266,6 +266,7 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
   if (D != 64 && D != 128) return HCP_ERR_UNSUPPORTED;
   if (!(a->scale > 0.f) || !std::isfinite(a->scale)) return HCP_ERR_INVALID;
   if (a->num_work < 0 || (a->num_work > 0 && a->work == nullptr)) return HCP_ERR_INVALID;
+  if (a->window < 0) return HCP_ERR_INVALID;
   if (a->q == nullptr || a->out == nullptr || a->q_rows < 0) return HCP_ERR_INVALID;
   if (a->q_row_stride < static_cast<int64_t>(H) * D || a->out_row_stride < static_cast<int64_t>(H) * D)
     return HCP_ERR_INVALID;
@@ -393,6 +394,7 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
   p.group = H / Hkv;
   p.block_size = want_paged ? a->block_size : 16;
   p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.window = a->window;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (size_t base = 0; base < order.size();) {

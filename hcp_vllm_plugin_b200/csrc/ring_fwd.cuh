@@ -136,6 +136,7 @@ struct FwdParams {
   int num_work;
   float scale_log2;
   int total_tiles;
+  int window;  // sliding window of causal segments, 0 = none
   int tile_off[kMaxWork + 1];
   FwdItem work[kMaxWork];
   hcp_kv_segment segs[kMaxSegs];
@@ -288,6 +289,22 @@ __device__ __forceinline__ int segment_keys(const hcp_kv_segment& sg, int q0, in
   return static_cast<int>(max(0ll, min(static_cast<long long>(sg.len), last_visible)));
 }
 
+// Sliding window of a causal segment (keys j with qpos - window < j <= qpos
+// visible): the segment as query rows q0, q0+1, ... see it, starting at the
+// first whole KV tile row q0 sees (a multiple of kBlockN, so of the block
+// size too); the keys below the window inside that tile are masked per row.
+// Non-causal segments and window 0 are returned as they are.
+__device__ __forceinline__ hcp_kv_segment window_trim(hcp_kv_segment sg, int q0, int window) {
+  if (window <= 0 || sg.causal_off < 0 || sg.src == HCP_SRC_NONE || sg.len <= 0) return sg;
+  const long long lo = static_cast<long long>(sg.causal_off) + q0 - window + 1;  // first key row q0 sees
+  if (lo < kBlockN) return sg;
+  const int skip = static_cast<int>(min(static_cast<long long>(sg.len), lo / kBlockN * kBlockN));
+  sg.start += skip;
+  sg.len -= skip;
+  sg.causal_off -= skip;
+  return sg;
+}
+
 template <int D>
 struct FwdSmem {
   static constexpr int kBoxBytes = 128 * 128;  // 128 rows x 64 elems x 2 B
@@ -299,7 +316,7 @@ struct FwdSmem {
   // segment table: tile prefix [kMaxItemSegs + 1], keys needed by query tile
   // A and by B [kMaxItemSegs] each, segment count, precise flags A and B
   static constexpr int kSegOff = kBarOff + 8 * kNumBars + 16;
-  static constexpr int kSegInts = (kMaxItemSegs + 1) + 2 * kMaxItemSegs + 3;
+  static constexpr int kSegInts = (kMaxItemSegs + 1) + 2 * kMaxItemSegs + 3 + 4 * kMaxItemSegs;
   static constexpr int kEnd = kSegOff + 4 * kSegInts;
   static constexpr int kBytes = kEnd + 1024;  // + alignment slack
 };
@@ -373,8 +390,8 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   int ka0 = 0, kb0 = 0, ka1 = 0, kb1 = 0, tiles0 = 0, tiles2 = 0;
   bool pre_a = false, pre_b = false;
   if constexpr (!LIST) {
-    sg0 = segs[0];
-    sg1 = segs[1];
+    sg0 = window_trim(segs[0], q0, p.window);
+    sg1 = window_trim(segs[1], q0, p.window);
     ka0 = segment_keys(sg0, q0, rows_a);
     kb0 = segment_keys(sg0, q0 + kBlockM, rows_b);
     ka1 = segment_keys(sg1, q0, rows_a);
@@ -392,6 +409,7 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   int* sg_need_a = sg_base + kMaxItemSegs + 1;
   int* sg_need_b = sg_need_a + kMaxItemSegs;
   int* sg_misc = sg_need_b + kMaxItemSegs;  // [0] segments, [1] precise A, [2] precise B
+  hcp_kv_segment* sg_trim = reinterpret_cast<hcp_kv_segment*>(sg_misc + 3);  // the segments, windowed
 
   // ---- setup
   if (LIST && threadIdx.x == 0) {
@@ -399,13 +417,15 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
     int tiles = 0, keys_a = 0, keys_b = 0;
     const int n_seg = min(wk.seg_count, kMaxItemSegs);
     for (int s = 0; s < n_seg; ++s) {
-      const int ka = segment_keys(segs[s], q0, rows_a), kb = segment_keys(segs[s], q0 + kBlockM, rows_b);
+      const hcp_kv_segment sg = window_trim(segs[s], q0, p.window);
+      sg_trim[s] = sg;
+      const int ka = segment_keys(sg, q0, rows_a), kb = segment_keys(sg, q0 + kBlockM, rows_b);
       sg_base[s] = tiles;
       sg_need_a[s] = ka;
       sg_need_b[s] = kb;
       tiles += (max(ka, kb) + kBlockN - 1) / kBlockN;
-      keys_a += segment_keys(segs[s], q0, 1);
-      keys_b += segment_keys(segs[s], q0 + kBlockM, 1);
+      keys_a += segment_keys(sg, q0, 1);
+      keys_b += segment_keys(sg, q0 + kBlockM, 1);
     }
     sg_base[n_seg] = tiles;
     sg_misc[0] = n_seg;
@@ -464,7 +484,7 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   };
   auto seg_at = [&](int s) -> hcp_kv_segment {
     if constexpr (!LIST) return s == 0 ? sg0 : sg1;
-    else return segs[s];
+    else return sg_trim[s];
   };
   auto tile_key0 = [&](int t) { return (t - seg_base(tile_seg(t))) * kBlockN; };
   // is KV tile t needed by query tile x (0 = A, 1 = B)?
@@ -777,16 +797,18 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
         int vis = seg.len - key0;
         if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
         vis = max(0, min(vis, kBlockN));
+        // keys [0, lo) of the tile are below the row's sliding window
+        const int lo = (p.window > 0 && seg.causal_off >= 0) ? seg.causal_off + qrow - p.window + 1 - key0 : 0;
 
         uint32_t sr[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           ptx::tmem_ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
         ptx::tmem_wait_ld();
-        if (vis < kBlockN) {
+        if (vis < kBlockN || lo > 0) {
 #pragma unroll
           for (int i = 0; i < 128; ++i)
-            if (i >= vis) sr[i] = __float_as_uint(-INFINITY);
+            if (i >= vis || i < lo) sr[i] = __float_as_uint(-INFINITY);
         }
         float mx8[8];
 #pragma unroll
@@ -894,16 +916,18 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
       int vis = seg.len - key0;
       if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
       vis = max(0, min(vis, kBlockN));
+      // keys [0, lo) of the tile are below the row's sliding window
+      const int lo = (p.window > 0 && seg.causal_off >= 0) ? seg.causal_off + qrow - p.window + 1 - key0 : 0;
 
       uint32_t sr[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         ptx::tmem_ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       ptx::tmem_wait_ld();
-      if (vis < kBlockN) {
+      if (vis < kBlockN || lo > 0) {
 #pragma unroll
         for (int i = 0; i < 128; ++i)
-          if (i >= vis) sr[i] = __float_as_uint(-INFINITY);
+          if (i >= vis || i < lo) sr[i] = __float_as_uint(-INFINITY);
       }
       float mx;
       if constexpr (kWide) {

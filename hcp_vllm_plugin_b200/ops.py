@@ -96,6 +96,7 @@ def ring_attn_fwd(
     merge_lse: torch.Tensor | None = None,
     ext=None,
     seg_list: np.ndarray | None = None,
+    window: int | None = None,
 ) -> None:
     """Fused ring-attention forward over a list of work items (``hcp_ring_attn_fwd``).
 
@@ -105,6 +106,8 @@ def ring_attn_fwd(
     8 extra contiguous (k, v) sources, named by segments as
     ``HCP_SRC_EXT0 + i``; ``seg_list``: int32 [n, 4] segments that
     ``HCP_SRC_LIST`` items point into (``(HCP_SRC_LIST, first, count, 0)``).
+    ``window``: sliding window of the causal segments (keys j with
+    ``qpos - window < j <= qpos``), None = none.
     """
     if not q.is_cuda:
         raise ValueError("q must be a CUDA tensor (no CPU path)")
@@ -174,6 +177,10 @@ def ring_attn_fwd(
         seg_list = np.ascontiguousarray(seg_list, dtype=np.int32).reshape(-1, 4)
         a.seg_list = seg_list.ctypes.data_as(ctypes.POINTER(C.HcpKvSegment))
         a.num_seg_list = seg_list.shape[0]
+    if window is not None:
+        if int(window) <= 0:
+            raise ValueError("window must be a positive number of keys (or None)")
+        a.window = int(window)
     work = np.ascontiguousarray(work, dtype=np.int32)
     a.work = work.ctypes.data_as(ctypes.POINTER(C.HcpAttnWork))
     a.num_work = work.shape[0]
@@ -187,9 +194,13 @@ def ring_attn_with_lse(
     v: torch.Tensor,
     scale: float,
     causal_offset: int | None,
+    window: int | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Flash attention with LSE output; drop-in for the reference's
-    ``ring_attn_with_lse`` (``hcp_vllm_plugin/ring_triton_attn.py:155-207``).
+    ``ring_attn_with_lse`` (``hcp_vllm_plugin/ring_triton_attn.py:155-207``),
+    and with ``window`` for its torch path's sliding window
+    (``_attn_with_lse``, ``ring_backend.py:366-406``: applied with a causal
+    offset only, as there).
 
     q [Tq, H, D], k/v [Tk, Hkv, D]; ``causal_offset`` = position of query 0 in
     the KV frame, ``None`` = non-causal.  Returns (out [Tq, H, D] in q's dtype,
@@ -205,7 +216,8 @@ def ring_attn_with_lse(
     if causal_offset is not None and causal_offset < 0:
         raise ValueError("causal_offset must be >= 0 or None")
     work = make_work([(0, tq, 0, 0, seg, None)])
-    ring_attn_fwd(q, work, scale=scale, num_kv_heads=num_kv_heads, out=out, lse=lse, k_a=k, v_a=v)
+    ring_attn_fwd(q, work, scale=scale, num_kv_heads=num_kv_heads, out=out, lse=lse, k_a=k, v_a=v,
+                  window=window)
     return out, lse
 
 

@@ -238,15 +238,17 @@ class HcpRingAttentionImpl(AttentionImpl):
             raise NotImplementedError("HCP ring backend: ALiBi not supported")
         if logits_soft_cap:
             raise NotImplementedError("HCP ring backend: soft cap not supported")
-        if sliding_window is not None:
-            # The reference serves windows with its fp32 torch path; this
-            # backend has no CPU path and its kernels have no window mask.
-            raise NotImplementedError("HCP ring backend: sliding window not supported")
+        if sliding_window is not None and int(sliding_window) <= 0:
+            raise ValueError("HCP ring backend: sliding window must be positive")
         if kv_cache_dtype not in ("auto", "bfloat16", "float16"):
             raise NotImplementedError(f"HCP ring backend: kv cache dtype {kv_cache_dtype}")
         if head_size not in (64, 128):
             raise NotImplementedError("HCP ring backend: head_size must be 64 or 128")
-        self.sliding_window = None
+        # As the reference's torch path (ring_backend.py:490-492, 786-826): the
+        # window applies to the causal (local) passes; staged peer chunks stay
+        # fully visible.  Decode rows then go through the prefill kernel,
+        # whose causal segments carry the window.
+        self.sliding_window = int(sliding_window) if sliding_window is not None else None
         self.num_queries_per_kv = self.num_heads // self.num_kv_heads
 
     # -- KV cache update -----------------------------------------------------
@@ -367,7 +369,10 @@ class HcpRingAttentionImpl(AttentionImpl):
         # The plan depends on lengths only (requests, staged chunks), which
         # every layer of a step shares: build it once per step and rebuild
         # just this layer's list of staged tensors.
-        sig = (block_size, split, excluded,
+        window = self.sliding_window
+        if window is not None and ring_rows:
+            raise NotImplementedError("HCP ring backend: the decode ring has no sliding window")
+        sig = (block_size, split, excluded, window is None,
                tuple((r, tuple(int(k.shape[0]) for k, _ in ch)) for r, ch in sorted(peers.items())))
         plans = getattr(attn_metadata, "_hcp_plans", None)
         if plans is None:
@@ -378,7 +383,8 @@ class HcpRingAttentionImpl(AttentionImpl):
                 pass
         plan = plans.get(sig)
         if plan is None:
-            plan = plan_layer(qsl, seq_lens, block_size, peers, split, exclude=excluded)
+            plan = plan_layer(qsl, seq_lens, block_size, peers, split, decode_kernel=window is None,
+                              exclude=excluded)
             if misaligned_paged_starts(plan, block_size):
                 raise ValueError("HCP ring backend: peer prefix length must be a multiple of the block size")
             plans[sig] = plan
@@ -399,7 +405,8 @@ class HcpRingAttentionImpl(AttentionImpl):
                     ext.append(peers[r][c])
             if grp.work.shape[0]:
                 ops.ring_attn_fwd(q, grp.work, scale=self.scale, num_kv_heads=self.num_kv_heads, out=out,
-                                  kv_cache=kv_cache, block_table=block_table, ext=ext, seg_list=grp.seg_list)
+                                  kv_cache=kv_cache, block_table=block_table, ext=ext, seg_list=grp.seg_list,
+                                  window=window)
                 IMPL_STATS["attn_cuda"] += 1
             if grp.decode.shape[0]:
                 ops.decode_splitkv(q, grp.decode, scale=self.scale, num_kv_heads=self.num_kv_heads, out=out,

@@ -116,6 +116,12 @@ typedef struct hcp_fwd_args {
    * when unused. */
   const hcp_kv_source* ext;   int32_t num_ext;     int32_t _pad5;
   const hcp_kv_segment* seg_list; int32_t num_seg_list; int32_t _pad6;
+  /* Sliding window, 0 = none: in every causal segment (causal_off >= 0) a
+   * query row at position qpos (causal_off + its row in the item) sees the
+   * keys j with qpos - window < j <= qpos; non-causal segments stay fully
+   * visible (the reference's _attn_with_lse window, applied to the local
+   * passes only: ring_backend.py:786-826). */
+  int32_t window;         int32_t _pad7;
 } hcp_fwd_args;
 
 /*

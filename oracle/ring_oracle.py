@@ -285,6 +285,7 @@ class RingBatch:
     scale: float
     staged: dict = field(default_factory=dict)  # request index -> (k_peer, v_peer)
     split_tokens: int = 0
+    window: int | None = None         # the impl's sliding_window (ring_backend.py:490-492)
 
 
 def ring_forward(batch: RingBatch, round_to_bf16: bool = True) -> np.ndarray:
@@ -303,7 +304,10 @@ def ring_forward(batch: RingBatch, round_to_bf16: bool = True) -> np.ndarray:
       attention over ``k_all[peer_end:]`` at offset ``qpos0 + n_a - peer_end``
       merged with non-causal attention over the peer KV (``:819-832``);
     * every result is cast to the output dtype (``o.to(output.dtype)``); with
-      ``round_to_bf16`` the returned float32 array holds those bf16 values.
+      ``round_to_bf16`` the returned float32 array holds those bf16 values;
+    * a sliding window applies to the causal passes only - the vanilla pass,
+      the ``n_a`` rows and the local pass - and not to the peer pass
+      (``:786, 815, 826`` pass ``self.sliding_window``, ``:829`` does not).
 
     Returns out [num_tokens, H, D] float32 (rows not covered stay 0).
     """
@@ -324,7 +328,7 @@ def ring_forward(batch: RingBatch, round_to_bf16: bool = True) -> np.ndarray:
                             batch.split_tokens)
         q_r = q_all[qs:qe]
         if plan.peer_end == 0:
-            o, _ = attn_with_lse(q_r, k_all, v_all, batch.scale, plan.qpos0)
+            o, _ = attn_with_lse(q_r, k_all, v_all, batch.scale, plan.qpos0, batch.window)
             out[qs:qe] = cast(o)
             continue
         if plan.peer_source == "staged":
@@ -333,13 +337,13 @@ def ring_forward(batch: RingBatch, round_to_bf16: bool = True) -> np.ndarray:
             k_peer, v_peer = k_all[: plan.peer_end], v_all[: plan.peer_end]
         n_a = plan.n_a
         if n_a > 0:
-            o_a, _ = attn_with_lse(q_r[:n_a], k_all, v_all, batch.scale, plan.qpos0)
+            o_a, _ = attn_with_lse(q_r[:n_a], k_all, v_all, batch.scale, plan.qpos0, batch.window)
             out[qs:qs + n_a] = cast(o_a)
         if n_a < tq:
             q_b = q_r[n_a:]
             o_loc, lse_loc = attn_with_lse(
                 q_b, k_all[plan.peer_end:], v_all[plan.peer_end:], batch.scale,
-                plan.qpos0 + n_a - plan.peer_end)
+                plan.qpos0 + n_a - plan.peer_end, batch.window)
             o_peer, lse_peer = attn_with_lse(q_b, k_peer, v_peer, batch.scale, None)
             out[qs + n_a:qe] = cast(lse_merge(o_loc, lse_loc, o_peer, lse_peer))
     return out

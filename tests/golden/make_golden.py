@@ -17,10 +17,14 @@ inputs and outputs as compressed ``.npz`` files next to this script:
   multi-chunk peer prefix.  The reference cache layout
   ``[num_blocks, 2, block_size, Hkv, D]`` is converted to
   ``[num_blocks, Hkv, block_size, 2*D]`` for storage.
+* ``window_case.npz`` (``--window``) - the same batch through a
+  ``HcpRingAttentionImpl`` built with ``sliding_window=20`` (the reference
+  applies the window to the causal passes, ``ring_backend.py:786-826``), and
+  ``_attn_with_lse`` with windows 1, 7 and 64 on causal cases.
 
 Usage (in a container holding the reference sources and vLLM)::
 
-    HCP_REFERENCE_ROOT=/path/to/hcp-vllm-plugin python tests/golden/make_golden.py
+    HCP_REFERENCE_ROOT=/path/to/hcp-vllm-plugin python tests/golden/make_golden.py [--window]
 """
 
 from __future__ import annotations
@@ -113,7 +117,7 @@ def merge_cases(attn_with_lse, lse_merge) -> dict:
     return out
 
 
-def forward_case(rb) -> dict:
+def forward_case(rb, window: int | None = None) -> dict:
     """Run the reference HcpRingAttentionImpl.forward on CPU over a small batch."""
     torch.manual_seed(2)
     h, hkv, d, bs = 28, 4, 128, 16
@@ -165,7 +169,7 @@ def forward_case(rb) -> dict:
             keys.append(ck)
         rb.map_request_peer(int(block_table[r, 0]), keys)
 
-    impl = rb.HcpRingAttentionImpl(h, d, scale, hkv)
+    impl = rb.HcpRingAttentionImpl(h, d, scale, hkv, sliding_window=window)
     meta = types.SimpleNamespace(
         num_actual_tokens=num_tokens,
         query_start_loc=torch.tensor(qsl, dtype=torch.int32),
@@ -191,8 +195,26 @@ def forward_case(rb) -> dict:
         seq_lens=np.array([tk for _, tk, _ in reqs], np.int64),
         peer_counts=np.array([0 if p is None else len(p) for _, _, p in reqs], np.int64),
         output=_u16(output),
+        window=np.array([0 if window is None else window], np.int64),
     )
     out.update(staged_np)
+    return out
+
+
+def window_kernel_cases(attn_with_lse) -> dict:
+    """``_attn_with_lse`` with a sliding window (H=28, Hkv=4, D=128, bf16)."""
+    torch.manual_seed(3)
+    out: dict[str, np.ndarray] = {}
+    for i, (tq, tk, off, w) in enumerate([(37, 37, 0, 1), (37, 512, 475, 7), (96, 300, 204, 64)]):
+        q = torch.randn(tq, 28, 128, dtype=torch.bfloat16)
+        k = torch.randn(tk, 4, 128, dtype=torch.bfloat16)
+        v = torch.randn(tk, 4, 128, dtype=torch.bfloat16)
+        o, lse = attn_with_lse(q, k, v, 128 ** -0.5, off, w)
+        rows = _rows(tq)
+        out[f"w{i}_q"], out[f"w{i}_k"], out[f"w{i}_v"] = _u16(q), _u16(k), _u16(v)
+        out[f"w{i}_rows"] = rows
+        out[f"w{i}_o"], out[f"w{i}_lse"] = o.numpy()[rows], lse.numpy()[:, rows]
+        out[f"w{i}_meta"] = np.array([tq, tk, off, w], np.int64)
     return out
 
 
@@ -206,6 +228,15 @@ def main() -> None:
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     from hcp_vllm_plugin import ring_backend as rb  # noqa: E402  (reference code)
 
+    if "--window" in sys.argv:
+        # the batch's inputs are those of forward_case.npz (same seed): keep
+        # only the windowed output
+        full = forward_case(rb, window=20)
+        case = {"output": full["output"], "window": full["window"]}
+        case.update(window_kernel_cases(rb._attn_with_lse))
+        np.savez_compressed(os.path.join(OUT_DIR, "window_case.npz"), **case)
+        print("window fixture written to", OUT_DIR)
+        return
     np.savez_compressed(os.path.join(OUT_DIR, "kernel_cases.npz"), **kernel_cases(rb._attn_with_lse))
     np.savez_compressed(os.path.join(OUT_DIR, "merge_cases.npz"),
                         **merge_cases(rb._attn_with_lse, rb._lse_merge))

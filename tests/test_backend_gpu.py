@@ -26,9 +26,23 @@ GOLD = os.path.join(os.path.dirname(__file__), "golden")
 
 
 def test_backend_forward_matches_reference_forward():
+    _backend_vs_reference_forward(None)
+
+
+def test_backend_sliding_window_matches_reference_forward():
+    """The same batch through an impl built with ``sliding_window=20``: the
+    reference's forward output with that window (``window_case.npz``); decode
+    rows then run through the prefill kernel's windowed causal segments."""
+    _backend_vs_reference_forward(20)
+
+
+def _backend_vs_reference_forward(window):
     from hcp_vllm_plugin_b200 import ring_backend as rb
     dev = torch.device("cuda:0")
     z = np.load(os.path.join(GOLD, "forward_case.npz"))
+    zw = np.load(os.path.join(GOLD, "window_case.npz")) if window else None
+    if window:
+        assert int(zw["window"][0]) == window
     h, hkv, d, bs, nreq, ntok = (int(x) for x in z["meta"])
     scale = float(z["scale"][0])
 
@@ -49,7 +63,7 @@ def test_backend_forward_matches_reference_forward():
             rb.stage_peer_kv(ck, layer_name, t16(z[f"peer{r}_{c}_k"]), t16(z[f"peer{r}_{c}_v"]))
             keys.append(ck)
         rb.map_request_peer(int(z["block_table"][r, 0]), keys)
-    impl = rb.HcpRingAttentionImpl(h, d, scale, hkv)
+    impl = rb.HcpRingAttentionImpl(h, d, scale, hkv, sliding_window=window)
     meta = types.SimpleNamespace(
         num_actual_tokens=ntok,
         query_start_loc=torch.tensor(z["query_start_loc"], dtype=torch.int32, device=dev),
@@ -66,10 +80,12 @@ def test_backend_forward_matches_reference_forward():
     torch.cuda.synchronize()
     rb.clear_peer_kv()
     assert len(meta._hcp_plans) == 1 and torch.equal(out, out2)
-    assert rb.IMPL_STATS["attn_cuda"] == 2 and rb.IMPL_STATS["decode_cuda"] == 2
+    # with a window the decode rows join the prefill launch
+    assert rb.IMPL_STATS["attn_cuda"] == 2 and rb.IMPL_STATS["decode_cuda"] == (0 if window else 2)
     assert rb.IMPL_STATS["peer_concat"] == 0  # the 3-chunk prefix is read where it is staged
     got = out[:ntok].float().cpu().numpy()
-    ref_out = ro.bf16_bits_to_f32(z["output"])  # the reference forward's own (bf16) output
+    # the reference forward's own (bf16) output
+    ref_out = ro.bf16_bits_to_f32((zw if window else z)["output"])
     # the fp32 values behind it: the oracle's restatement of the same forward
     staged = {}
     for r in range(nreq):
@@ -79,9 +95,10 @@ def test_backend_forward_matches_reference_forward():
                          np.concatenate([ro.bf16_bits_to_f32(z[f"peer{r}_{c}_v"]) for c in range(n)]))
     batch = ro.RingBatch(query=ro.bf16_bits_to_f32(z["query"]), cache=ro.bf16_bits_to_f32(z["cache"]),
                          block_table=z["block_table"], query_start_loc=z["query_start_loc"],
-                         seq_lens=z["seq_lens"], scale=scale, staged=staged)
+                         seq_lens=z["seq_lens"], scale=scale, staged=staged, window=window)
     want = ro.ring_forward(batch, round_to_bf16=False)
-    print(P.check_out(got, want, "backend forward vs reference forward", ref_out=ref_out).line())
+    name = "backend forward vs reference forward" + (f" (window {window})" if window else "")
+    print(P.check_out(got, want, name, ref_out=ref_out).line())
     assert (out[ntok:].float() == 0).all()  # padding rows untouched
 
 

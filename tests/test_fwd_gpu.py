@@ -273,3 +273,75 @@ def test_segment_lists_over_separate_chunks(dev):
         want, want_lse = ro.attn_with_lse(_f(b["q"][qs:qs + L]), k, v, D128 ** -0.5, sum(chunk_lens[r]))
         P.check_out(_f(out[qs:qs + L]), want, f"segment list request {r}")
         P.check_lse(_f(lse[:, qs:qs + L]), want_lse, f"segment list request {r}")
+
+
+@pytest.mark.parametrize("tq,tk,off,window", [
+    (1000, 1000, 0, 1), (1000, 1000, 0, 100), (1000, 1000, 0, 200), (1000, 1000, 0, 700),
+    (300, 2000, 1700, 333), (1, 4096, 4095, 129), (513, 513, 0, 128)])
+def test_sliding_window_contiguous(dev, tq, tk, off, window):
+    """A causal segment with a sliding window (keys j with qpos - window < j <=
+    qpos) vs the oracle's ``_attn_with_lse(window=...)`` restatement; whole KV
+    tiles below a CTA's window are skipped, the edge tile is masked per row."""
+    from hcp_vllm_plugin_b200.ops import ring_attn_with_lse
+    g = torch.Generator(device="cpu").manual_seed(tq + tk + window)
+    q = torch.randn(tq, H28, D128, generator=g).bfloat16()
+    k = torch.randn(tk, HKV4, D128, generator=g).bfloat16()
+    v = torch.randn(tk, HKV4, D128, generator=g).bfloat16()
+    o, lse = ring_attn_with_lse(q.to(dev), k.to(dev), v.to(dev), D128 ** -0.5, off, window=window)
+    torch.cuda.synchronize()
+    rows = np.unique(np.r_[np.linspace(0, tq - 1, min(tq, 96)).astype(int), [tq - 1]])
+    want_o, want_lse = ro.attn_with_lse(_f(q)[rows[0]:rows[-1] + 1], _f(k), _f(v), D128 ** -0.5,
+                                        off + int(rows[0]), window)
+    sel = rows - rows[0]
+    name = f"window/{tq}x{tk}@{off}/w{window}"
+    st = P.check_out(_f(o)[rows], want_o[sel], name)
+    P.check_lse(_f(lse)[:, rows], want_lse[:, sel], name)
+    print(st.line())
+
+
+@pytest.mark.parametrize("window", [48, 300, 1500])
+def test_sliding_window_paged_with_peers_and_lists(dev, window):
+    """A cfg1-shaped batch with a window: the paged local segment is windowed,
+    the contiguous peer prefix stays fully visible (the reference's forward,
+    ring_backend.py:819-832); one request's keys come as a segment list (the
+    list kernel) over two extra sources plus the paged local keys."""
+    from hcp_vllm_plugin_b200 import _capi as C, ops
+    lens, peer = [700, 129, 1, 2048], 512
+    b = P.paged_batch(lens, peer, seed=11)
+    E = C.HCP_SRC_EXT0
+    kp, vp = b["kp"], b["vp"]
+    items, seg_list, ext = [], [], []
+    for r, L in enumerate(lens):
+        qs = int(b["qsl"][r])
+        loc = (C.HCP_SRC_PAGED, peer, L, 0)
+        if r == 0:
+            # the peer prefix as two separately allocated chunks: a list item
+            half = peer // 2
+            for c in range(2):
+                sl = slice(r * peer + c * half, r * peer + (c + 1) * half)
+                ext.append((kp[sl].contiguous().to(dev), vp[sl].contiguous().to(dev)))
+            seg_list += [(E + 0, 0, half, -1), (E + 1, 0, half, -1), loc]
+            items.append((qs, L, r, qs, (C.HCP_SRC_LIST, 0, 3, 0), None))
+        else:
+            items.append((qs, L, r, qs, (C.HCP_SRC_A, r * peer, peer, -1), loc))
+    q = b["q"].to(dev)
+    out = torch.empty_like(q)
+    lse = torch.empty(H28, q.shape[0], dtype=torch.float32, device=dev)
+    ops.ring_attn_fwd(q, ops.make_work(items), scale=D128 ** -0.5, num_kv_heads=HKV4, out=out, lse=lse,
+                      k_a=kp.to(dev), v_a=vp.to(dev), kv_cache=b["cache"].to(dev),
+                      block_table=torch.from_numpy(b["bt"]).to(dev), ext=ext, seg_list=np.array(seg_list),
+                      window=window)
+    torch.cuda.synchronize()
+    for r, L in enumerate(lens):
+        qs = int(b["qsl"][r])
+        kl, vl = P.paged_local_kv(b, r)
+        qr = _f(b["q"][qs:qs + L])
+        o_loc, l_loc = ro.attn_with_lse(qr, _f(kl), _f(vl), D128 ** -0.5, 0, window)
+        o_peer, l_peer = ro.attn_with_lse(qr, _f(kp[r * peer:(r + 1) * peer]), _f(vp[r * peer:(r + 1) * peer]),
+                                          D128 ** -0.5, None)
+        want = ro.lse_merge(o_loc, l_loc, o_peer, l_peer)
+        m = np.maximum(l_loc, l_peer)
+        want_lse = m + np.log(np.exp(l_loc - m) + np.exp(l_peer - m))
+        name = f"window {window} paged request {r} ({'list' if r == 0 else 'inline'})"
+        P.check_out(_f(out[qs:qs + L]), want, name)
+        P.check_lse(_f(lse[:, qs:qs + L]), want_lse, name)

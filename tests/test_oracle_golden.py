@@ -156,3 +156,32 @@ def test_bf16_rounding():
     assert r[0] == 1.0 and r[1] == 1.0  # tie to even
     assert r[2] == np.float32(1.015625)
     assert r[3] == -2.5
+
+
+def test_window_attention_matches_reference():
+    """``_attn_with_lse`` with a sliding window (``ring_backend.py:391-398``)."""
+    z = np.load(os.path.join(GOLD, "window_case.npz"))
+    for i in range(3):
+        tq, tk, off, w = (int(x) for x in z[f"w{i}_meta"])
+        q, k, v = (ro.bf16_bits_to_f32(z[f"w{i}_{n}"]) for n in "qkv")
+        rows = z[f"w{i}_rows"]
+        o, lse = ro.attn_with_lse(q, k, v, 128 ** -0.5, off, w)
+        np.testing.assert_allclose(o[rows], z[f"w{i}_o"], atol=2e-6, rtol=1e-5)
+        np.testing.assert_allclose(lse[:, rows], z[f"w{i}_lse"], atol=2e-6, rtol=1e-6)
+        assert w < tk  # the window cuts keys in every case
+
+
+def test_ring_forward_with_window_matches_reference_forward():
+    """The reference forward built with ``sliding_window=20``: the window on
+    the causal passes only, the staged peer chunks fully visible."""
+    z, batch = _forward_batch()
+    zw = np.load(os.path.join(GOLD, "window_case.npz"))
+    batch.window = int(zw["window"][0])
+    want = ro.bf16_bits_to_f32(zw["output"])
+    got = ro.ring_forward(batch, round_to_bf16=True)
+    diff = np.abs(got - want)
+    ulp = np.abs(want) * 2.0 ** -7 + 1e-30
+    assert (diff <= np.maximum(1e-6, ulp)).all()
+    assert (diff > 1e-6).mean() < 1e-3
+    # the window changed the result (it is not a no-op on this batch)
+    assert np.abs(want - ro.bf16_bits_to_f32(z["output"])).max() > 0.05
