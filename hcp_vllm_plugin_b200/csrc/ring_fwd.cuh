@@ -281,21 +281,29 @@ __device__ __forceinline__ float2 unpack2(uint32_t u) {
   }
 }
 
+// In-kernel marker of a non-causal segment (see cta_segment).
+constexpr int kNonCausal = -2147483647 - 1;
+
 // Keys of segment `sg` visible to the valid rows [q0, q0+rows) of a query tile.
 __device__ __forceinline__ int segment_keys(const hcp_kv_segment& sg, int q0, int rows) {
   if (rows <= 0 || sg.src == HCP_SRC_NONE || sg.len <= 0) return 0;
-  if (sg.causal_off < 0) return sg.len;
+  if (sg.causal_off == kNonCausal) return sg.len;
   const long long last_visible = static_cast<long long>(sg.causal_off) + q0 + rows;  // exclusive
   return static_cast<int>(max(0ll, min(static_cast<long long>(sg.len), last_visible)));
 }
 
-// Sliding window of a causal segment (keys j with qpos - window < j <= qpos
-// visible): the segment as query rows q0, q0+1, ... see it, starting at the
-// first whole KV tile row q0 sees (a multiple of kBlockN, so of the block
+// A segment as the CTA whose rows start at q0 uses it.  Non-causal segments
+// (causal_off < 0 at the ABI) get the in-kernel marker kNonCausal, since a
+// trimmed causal segment may have a negative offset.  With a sliding window
+// (keys j with qpos - window < j <= qpos visible) a causal segment starts at
+// the first whole KV tile row q0 sees (a multiple of kBlockN, so of the block
 // size too); the keys below the window inside that tile are masked per row.
-// Non-causal segments and window 0 are returned as they are.
-__device__ __forceinline__ hcp_kv_segment window_trim(hcp_kv_segment sg, int q0, int window) {
-  if (window <= 0 || sg.causal_off < 0 || sg.src == HCP_SRC_NONE || sg.len <= 0) return sg;
+__device__ __forceinline__ hcp_kv_segment cta_segment(hcp_kv_segment sg, int q0, int window) {
+  if (sg.causal_off < 0) {
+    sg.causal_off = kNonCausal;
+    return sg;
+  }
+  if (window <= 0 || sg.src == HCP_SRC_NONE || sg.len <= 0) return sg;
   const long long lo = static_cast<long long>(sg.causal_off) + q0 - window + 1;  // first key row q0 sees
   if (lo < kBlockN) return sg;
   const int skip = static_cast<int>(min(static_cast<long long>(sg.len), lo / kBlockN * kBlockN));
@@ -390,8 +398,8 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
   int ka0 = 0, kb0 = 0, ka1 = 0, kb1 = 0, tiles0 = 0, tiles2 = 0;
   bool pre_a = false, pre_b = false;
   if constexpr (!LIST) {
-    sg0 = window_trim(segs[0], q0, p.window);
-    sg1 = window_trim(segs[1], q0, p.window);
+    sg0 = cta_segment(segs[0], q0, p.window);
+    sg1 = cta_segment(segs[1], q0, p.window);
     ka0 = segment_keys(sg0, q0, rows_a);
     kb0 = segment_keys(sg0, q0 + kBlockM, rows_b);
     ka1 = segment_keys(sg1, q0, rows_a);
@@ -417,7 +425,7 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
     int tiles = 0, keys_a = 0, keys_b = 0;
     const int n_seg = min(wk.seg_count, kMaxItemSegs);
     for (int s = 0; s < n_seg; ++s) {
-      const hcp_kv_segment sg = window_trim(segs[s], q0, p.window);
+      const hcp_kv_segment sg = cta_segment(segs[s], q0, p.window);
       sg_trim[s] = sg;
       const int ka = segment_keys(sg, q0, rows_a), kb = segment_keys(sg, q0 + kBlockM, rows_b);
       sg_base[s] = tiles;
@@ -795,10 +803,10 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
         const int key0 = tile_key0(t);
         const hcp_kv_segment seg = seg_at(tile_seg(t));
         int vis = seg.len - key0;
-        if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
+        if (seg.causal_off != kNonCausal) vis = min(vis, seg.causal_off + qrow - key0 + 1);
         vis = max(0, min(vis, kBlockN));
         // keys [0, lo) of the tile are below the row's sliding window
-        const int lo = (p.window > 0 && seg.causal_off >= 0) ? seg.causal_off + qrow - p.window + 1 - key0 : 0;
+        const int lo = (p.window > 0 && seg.causal_off != kNonCausal) ? seg.causal_off + qrow - p.window + 1 - key0 : 0;
 
         uint32_t sr[128];
 #pragma unroll
@@ -914,10 +922,10 @@ __global__ void __launch_bounds__(V >= 3 ? kThreadsWide : kThreads, 1)
       const int key0 = tile_key0(t);
       const hcp_kv_segment seg = seg_at(tile_seg(t));
       int vis = seg.len - key0;
-      if (seg.causal_off >= 0) vis = min(vis, seg.causal_off + qrow - key0 + 1);
+      if (seg.causal_off != kNonCausal) vis = min(vis, seg.causal_off + qrow - key0 + 1);
       vis = max(0, min(vis, kBlockN));
       // keys [0, lo) of the tile are below the row's sliding window
-      const int lo = (p.window > 0 && seg.causal_off >= 0) ? seg.causal_off + qrow - p.window + 1 - key0 : 0;
+      const int lo = (p.window > 0 && seg.causal_off != kNonCausal) ? seg.causal_off + qrow - p.window + 1 - key0 : 0;
 
       uint32_t sr[128];
 #pragma unroll
