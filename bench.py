@@ -655,12 +655,13 @@ def reference_gpu_side(dev, pk) -> dict:
 
 def fwd_issuer_variants(seq: int) -> dict:
     """The forward kernel on one ``seq``-token causal launch in each variant
-    (``HCP_FWD_VARIANT``): 0 the default mbarrier MMA issuer, 1 the
+    (``HCP_FWD_VARIANT``): 0 the mbarrier MMA issuer on 320 threads, 1 the
     named-barrier issuer, 2 variant 1 with a quarter of the exponentials on
     the FMA pipe, 3-5 the mbarrier issuer on 384 threads with setmaxnreg
     register split and packed f32x2 softmax math, with 1/4, 3/8 and none of
-    the exponentials on the FMA pipe, 6 the named-barrier issuer on 384 threads
-    with the setmaxnreg split.  Each runs in a fresh process, since the
+    the exponentials on the FMA pipe (5 is the default), 6 the named-barrier
+    issuer on 384 threads with the setmaxnreg split.  Each runs in a fresh
+    process, since the
     library reads the switch once per process.  Reported beside the headline
     only."""
     out = {}

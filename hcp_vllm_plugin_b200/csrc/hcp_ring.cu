@@ -107,12 +107,14 @@ bool g_attr_done[2][2][8][64];  // variants 0-6, and 7 for the LIST kernel
 bool g_dec_attr_done[2][2][64];
 
 // Forward kernel variant (read once per process): HCP_FWD_VARIANT=0..6, or
-// HCP_FWD_NAMED_BARRIERS=1 (1) / HCP_FWD_POLY_EXP2=1 (2).  0 - the mbarrier
-// MMA issuer; 1 - the named-barrier issuer; 2 - 1 with a quarter of the
-// exponentials on the FMA pipe; 3, 4, 5 - the mbarrier issuer on 384 threads
-// with the registers split by setmaxnreg and packed f32x2 softmax math, with
-// a quarter, three eighths or none of the exponentials on the FMA pipe; 6 -
-// the named-barrier issuer on 384 threads with the setmaxnreg split.
+// HCP_FWD_NAMED_BARRIERS=1 (1) / HCP_FWD_POLY_EXP2=1 (2); default 5, the
+// fastest measured (16k / 32k causal launches: +2.2% / +2.3% over 0).  0 -
+// the mbarrier MMA issuer on 320 threads; 1 - the named-barrier issuer; 2 -
+// 1 with a quarter of the exponentials on the FMA pipe; 3, 4, 5 - the
+// mbarrier issuer on 384 threads with the registers split by setmaxnreg and
+// packed f32x2 softmax math, with a quarter, three eighths or none of the
+// exponentials on the FMA pipe; 6 - the named-barrier issuer on 384 threads
+// with the setmaxnreg split.
 int fwd_variant() {
   static const int v = [] {
     auto on = [](const char* name) {
@@ -121,7 +123,7 @@ int fwd_variant() {
     };
     const char* e = std::getenv("HCP_FWD_VARIANT");
     if (e != nullptr && e[0] >= '0' && e[0] <= '6' && e[1] == 0) return e[0] - '0';
-    return on("HCP_FWD_POLY_EXP2") ? 2 : on("HCP_FWD_NAMED_BARRIERS") ? 1 : 0;
+    return on("HCP_FWD_POLY_EXP2") ? 2 : on("HCP_FWD_NAMED_BARRIERS") ? 1 : 5;
   }();
   return v;
 }
@@ -162,9 +164,9 @@ int launch_fwd(const FwdParams& p, int grid, cudaStream_t st, bool list) {
     case 2: return launch_fwd<D, F16, 2>(p, grid, st);
     case 3: return launch_fwd<D, F16, 3>(p, grid, st);
     case 4: return launch_fwd<D, F16, 4>(p, grid, st);
-    case 5: return launch_fwd<D, F16, 5>(p, grid, st);
     case 6: return launch_fwd<D, F16, 6>(p, grid, st);
-    default: return launch_fwd<D, F16, 0>(p, grid, st);
+    case 0: return launch_fwd<D, F16, 0>(p, grid, st);
+    default: return launch_fwd<D, F16, 5>(p, grid, st);
   }
 }
 
