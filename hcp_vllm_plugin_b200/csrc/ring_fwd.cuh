@@ -11,7 +11,8 @@
 // bound by operand traffic (L2 -> shared memory -> tensor core), and sharing
 // halves it per FLOP.
 //
-// Warp roles (320 threads):
+// Warp roles (320 threads; 384 in variants 3-6, warps 10-11 without a role,
+// so setmaxnreg can split the registers per warpgroup):
 //   warps 0-3  softmax / O correction / epilogue of query tile A
 //   warps 4-7  the same for query tile B.  Thread (w, lane) owns row
 //              32*(w%4)+lane of its tile, which is that TMEM lane.
