@@ -89,3 +89,42 @@ def test_outbox_pulls_stay_inside_the_owners_outbox():
                     # parity halves are disjoint
                     half = size[r] // 2
                     assert (off >= half) == (par == 1) and (off + n <= half) == (par == 0)
+
+
+def _model_layer_time(world: int, chunk: int, slots: int = 2, xfer: float = 0.01) -> float:
+    """Per-layer time of the hop schedule in units of one C x C block of
+    attention work, when a chunk lands ``xfer`` after both its owner and its
+    receiver are ready and a receive slot frees when the launch that read it
+    ends (the copy-engine transport: waiting holds no SMs).  The own causal
+    launch (0.5 units) fills the gaps of the hop stream."""
+    from hcp_vllm_plugin_b200.ring_schedule import hop_schedule
+
+    plan = plan_balanced(world, chunk)
+    end = {}
+    for x in range(world):
+        give = plan.rows_given(x)
+        owner = plan.helped_owner(x)
+        g = plan.rows_given(owner) if owner is not None else 0
+        t, busy, first, free = 0.0, 0.0, True, {}
+        for hp in hop_schedule(plan, x, slots):
+            if hp.recv_chunk is None:
+                continue
+            rows = (chunk - give if hp.own_rows else 0) + (g * (2 if first else 1) if hp.helper_rows else 0)
+            start = max(t, free.get(hp.slot, 0.0) + xfer)
+            t = start + rows / chunk
+            busy += rows / chunk
+            free[hp.slot] = t
+            first = False
+        # the causal launch runs in the gaps; whatever is left runs after
+        gaps = t - busy
+        end[x] = t + max(0.0, 0.5 - gaps)
+    return max(end.values())
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 5, 6, 8])
+def test_hop_schedule_model_is_balanced(world):
+    """With waits that hold no SMs, the balanced plan's hop schedule comes
+    within 3% of the ideal per-layer time (world / 2 blocks of C x C work)."""
+    t = _model_layer_time(world, 16384)
+    ideal = world / 2.0
+    assert t <= ideal * 1.03 + 0.02, (world, t, ideal)
