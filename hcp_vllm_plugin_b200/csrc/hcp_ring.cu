@@ -343,6 +343,43 @@ extern "C" int hcp_ring_attn_fwd(const hcp_fwd_args* a, void* stream) {
     item_segs.push_back(std::move(sg));
   }
   if (items.empty()) return HCP_OK;
+  // When every 256-row block of every item fits one launch as an item of its
+  // own, split them: the launch then runs the blocks in one heaviest-first
+  // order across requests (with whole items, a request's light blocks ran
+  // before the next request's heavy ones and lengthened the last wave).  A
+  // block starting at row r0 of its item sees its causal segments at offset
+  // causal_off + r0; the results are those of the whole item.
+  {
+    int64_t blocks = 0, segs = 0;
+    bool fits = true;
+    for (size_t i = 0; i < items.size(); ++i) {
+      const int64_t nb = (items[i].q_len + kCtaRows - 1) / kCtaRows;
+      blocks += nb;
+      segs += nb * static_cast<int64_t>(item_segs[i].size());
+      for (const hcp_kv_segment& s : item_segs[i])
+        if (s.causal_off >= 0 && static_cast<int64_t>(s.causal_off) + items[i].q_len > INT32_MAX) fits = false;
+    }
+    if (fits && items.size() > 1 && blocks > static_cast<int64_t>(items.size()) && blocks <= kMaxWork &&
+        segs <= kMaxSegs) {
+      std::vector<hcp_attn_work> split;
+      std::vector<std::vector<hcp_kv_segment>> split_segs;
+      for (size_t i = 0; i < items.size(); ++i) {
+        for (int r0 = 0; r0 < items[i].q_len; r0 += kCtaRows) {
+          hcp_attn_work w = items[i];
+          w.q_start += r0;
+          w.lse_col += r0;
+          w.q_len = std::min(kCtaRows, items[i].q_len - r0);
+          std::vector<hcp_kv_segment> sg = item_segs[i];
+          for (hcp_kv_segment& s : sg)
+            if (s.src != HCP_SRC_NONE && s.causal_off >= 0) s.causal_off += r0;
+          split.push_back(w);
+          split_segs.push_back(std::move(sg));
+        }
+      }
+      items.swap(split);
+      item_segs.swap(split_segs);
+    }
+  }
   std::vector<int> order(items.size());
   for (size_t i = 0; i < items.size(); ++i) {
     order[i] = static_cast<int>(i);
