@@ -157,14 +157,17 @@ class RingPrefill:
     def _open_outboxes(self) -> None:
         """Allocate this rank's outbox (two parity halves of [K | V | Q rows
         [0, give)]), export it, and map the outboxes of the ranks whose chunk
-        or Q rows this rank reads."""
+        or Q rows this rank reads.  Collective.  If any rank cannot export
+        or map (memory that CUDA IPC cannot share, e.g. an allocator with
+        expandable segments), every rank falls back to the p2p transport
+        together, so all take the same collective steps."""
         c, hkv, h, d = self.chunk, self.Hkv, self.H, self.D
         self.outbox = torch.empty(2, 2 * c * hkv * d + self.give * h * d, dtype=self.dtype, device=self.device)
         handle = (ctypes.c_uint8 * 64)()
         offset = ctypes.c_int64()
         lib = C.load()
-        C.check(lib.hcp_ipc_export(self.outbox.data_ptr(), handle, ctypes.byref(offset)), "hcp_ipc_export")
-        mine = (bytes(handle).hex(), int(offset.value))
+        rc = lib.hcp_ipc_export(self.outbox.data_ptr(), handle, ctypes.byref(offset))
+        mine = (bytes(handle).hex(), int(offset.value)) if rc == C.HCP_OK else None
         allx: list = [None] * self.world
         dist.all_gather_object(allx, mine, group=self.group)
         need = {hp.recv_chunk for hp in self.hops if hp.recv_chunk is not None}
@@ -173,12 +176,23 @@ class RingPrefill:
         self._elt = self.outbox.element_size()
         self._peer_box: dict[int, int] = {}
         dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
-        for r in sorted(need):
-            hx, off = allx[r]
-            base = ctypes.c_void_p()
-            C.check(lib.hcp_ipc_open(bytes.fromhex(hx), dev, ctypes.byref(base)), "hcp_ipc_open")
-            self._peer_bases.append(base.value)
-            self._peer_box[r] = base.value + off
+        ok = all(x is not None for x in allx)
+        if ok:
+            for r in sorted(need):
+                hx, off = allx[r]
+                base = ctypes.c_void_p()
+                if lib.hcp_ipc_open(bytes.fromhex(hx), dev, ctypes.byref(base)) != C.HCP_OK:
+                    ok = False
+                    break
+                self._peer_bases.append(base.value)
+                self._peer_box[r] = base.value + off
+        oks: list = [None] * self.world
+        dist.all_gather_object(oks, ok, group=self.group)
+        if not all(oks):
+            self.close()
+            self.outbox = None
+            self.transport = "p2p"
+            return
         self._sig = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._parity = 0
 

@@ -102,3 +102,76 @@ def test_ring_prefill_schedule_gloo(world, seq):
     assert err < 1e-4 and lerr < 1e-4, (err, lerr)
     if world in (2, 4):
         assert give, "balanced plan must hand rows to a light partner"
+
+
+class _FakeIpcLib:
+    """Stand-in for the library's CUDA IPC calls: ``fail_export`` /
+    ``fail_open`` make this rank's export or mapping fail."""
+
+    def __init__(self, fail_export=False, fail_open=False):
+        self.fail_export, self.fail_open, self.closed = fail_export, fail_open, []
+
+    def hcp_ipc_export(self, ptr, handle, offset):
+        return 1 if self.fail_export else 0
+
+    def hcp_ipc_open(self, handle, dev, base):
+        if self.fail_open:
+            return 1
+        base._obj.value = 4096 if hasattr(base, "_obj") else 4096
+        return 0
+
+    def hcp_ipc_close(self, b):
+        self.closed.append(b)
+        return 0
+
+
+def _transport_worker(rank, world, port, fail_rank, mode, result_q):
+    import types
+
+    from hcp_vllm_plugin_b200 import _capi as C
+    from hcp_vllm_plugin_b200.ring_runner import RingPrefill
+    from hcp_vllm_plugin_b200.ring_schedule import hop_schedule, plan_balanced
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lib = _FakeIpcLib(fail_export=(mode == "export" and rank == fail_rank),
+                          fail_open=(mode == "open" and rank == fail_rank))
+        C.load = lambda: lib
+        plan = plan_balanced(world, 256)
+        me = types.SimpleNamespace(
+            chunk=256, Hkv=HKV, H=H, D=D, dtype=torch.float32, device=torch.device("cpu", 0), world=world,
+            group=None, plan=plan, give=plan.rows_given(rank), owner=plan.helped_owner(rank),
+            owner_give=plan.rows_given(plan.helped_owner(rank)) if plan.helped_owner(rank) is not None else 0,
+            hops=hop_schedule(plan, rank), transport="ce", _peer_bases=[])
+        me.close = types.MethodType(RingPrefill.close, me)
+        RingPrefill._open_outboxes(me)
+        result_q.put((rank, me.transport))
+    except BaseException as e:  # noqa: BLE001 - reported to the test
+        result_q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["none", "export", "open"])
+def test_ce_transport_falls_back_together(mode):
+    """When one rank cannot export or map an outbox (memory CUDA IPC cannot
+    share), every rank switches to the p2p transport, so all keep taking the
+    same collective steps; otherwise all stay on ce."""
+    world = 4
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_transport_worker, args=(r, world, port, 3, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=60) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = "ce" if mode == "none" else "p2p"
+    assert got == {r: want for r in range(world)}
