@@ -110,3 +110,19 @@ def test_plan_split_tokens_and_misalignment():
     k = torch.zeros(20, 2, 64)
     plan = plan_layer([0, 10], [50], 16, {0: [(k, k)]})
     assert misaligned_paged_starts(plan, 16)
+
+
+def test_plan_without_decode_kernel_puts_decode_rows_in_prefill_items():
+    """With a sliding window the backend plans without the split-KV decode
+    kernel: the single-token request becomes a prefill item whose local
+    segment is causal at offset qpos0 - peer_end (the window applies to it in
+    the kernel), its staged chunk stays non-causal."""
+    z = np.load(os.path.join(GOLD, "forward_case.npz"))
+    peers = _peers_from_fixture(z)
+    plan = plan_layer(z["query_start_loc"], z["seq_lens"], 16, peers, decode_kernel=False)
+    assert plan.decode.shape[0] == 0 and plan.stats["decode_rows"] == 0
+    w = {tuple(x[:2]): x for x in plan.work}
+    x = w[(104, 1)]
+    E = C.HCP_SRC_EXT0
+    assert list(x[4:8]) == [E + 2, 0, 48, -1]
+    assert list(x[8:12]) == [C.HCP_SRC_PAGED, 48, 97 - 48, 96 - 48]
