@@ -660,13 +660,14 @@ def fwd_issuer_variants(seq: int) -> dict:
     the FMA pipe, 3-5 the mbarrier issuer on 384 threads with setmaxnreg
     register split and packed f32x2 softmax math, with 1/4, 3/8 and none of
     the exponentials on the FMA pipe (5 is the default), 6 the named-barrier
-    issuer on 384 threads with the setmaxnreg split.  Each runs in a fresh
-    process, since the
-    library reads the switch once per process.  Reported beside the headline
-    only."""
+    issuer on 384 threads with the setmaxnreg split, 7 variant 5 as a
+    persistent kernel (one CTA per SM over a static list of 256-row blocks).
+    Each runs in a fresh process, since the library reads the switch once
+    per process.  Reported beside the headline only."""
     out = {}
     names = ("mbarrier_issuer", "named_barrier_issuer", "named_barrier_poly_exp2",
-             "wide_poly_quarter", "wide_poly_three_eighths", "wide_no_poly", "named_barrier_wide")
+             "wide_poly_quarter", "wide_poly_three_eighths", "wide_no_poly", "named_barrier_wide",
+             "wide_persistent")
     for variant, name in enumerate(names):
         env = dict(os.environ, HCP_FWD_VARIANT=str(variant))
         cmd = [sys.executable, os.path.abspath(__file__), "--kernel", "fwd", "--seq", str(seq), "--iters", "5"]

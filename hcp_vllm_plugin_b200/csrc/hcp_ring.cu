@@ -19,6 +19,7 @@
 
 #include "hcp_ring.h"
 #include "ring_fwd.cuh"
+#include "ring_fwd_persistent.cuh"
 #include "decode.cuh"
 #include "cache.cuh"
 #include "merge.cuh"
@@ -106,7 +107,7 @@ std::mutex g_attr_mu;
 bool g_attr_done[2][2][8][64];  // variants 0-6, and 7 for the LIST kernel
 bool g_dec_attr_done[2][2][64];
 
-// Forward kernel variant (read once per process): HCP_FWD_VARIANT=0..6, or
+// Forward kernel variant (read once per process): HCP_FWD_VARIANT=0..7, or
 // HCP_FWD_NAMED_BARRIERS=1 (1) / HCP_FWD_POLY_EXP2=1 (2); default 5, the
 // fastest measured (16k / 32k causal launches: +2.2% / +2.3% over 0).  0 -
 // the mbarrier MMA issuer on 320 threads; 1 - the named-barrier issuer; 2 -
@@ -114,7 +115,8 @@ bool g_dec_attr_done[2][2][64];
 // mbarrier issuer on 384 threads with the registers split by setmaxnreg and
 // packed f32x2 softmax math, with a quarter, three eighths or none of the
 // exponentials on the FMA pipe; 6 - the named-barrier issuer on 384 threads
-// with the setmaxnreg split.
+// with the setmaxnreg split; 7 - variant 5 as a persistent kernel, one CTA
+// per SM running a static list of 256-row blocks (ring_fwd_persistent.cuh).
 int fwd_variant() {
   static const int v = [] {
     auto on = [](const char* name) {
@@ -122,7 +124,7 @@ int fwd_variant() {
       return e != nullptr && e[0] == '1';
     };
     const char* e = std::getenv("HCP_FWD_VARIANT");
-    if (e != nullptr && e[0] >= '0' && e[0] <= '6' && e[1] == 0) return e[0] - '0';
+    if (e != nullptr && e[0] >= '0' && e[0] <= '7' && e[1] == 0) return e[0] - '0';
     return on("HCP_FWD_POLY_EXP2") ? 2 : on("HCP_FWD_NAMED_BARRIERS") ? 1 : 5;
   }();
   return v;
@@ -155,11 +157,46 @@ int launch_fwd(const FwdParams& p, int grid, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
 }
 
+bool g_persist_attr_done[2][2][64];
+int g_sm_count[64];
+
+// Variant 7: one CTA per SM (at most one per block x head), each running its
+// share of the blocks in the persistent kernel's static order.
+template <int D, bool F16>
+int launch_fwd_persistent(const FwdParams& p, int jobs, cudaStream_t st) {
+  constexpr int smem = fwd_persistent_smem_bytes<D>();
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HCP_ERR_CUDA;
+  int sms = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    if (!g_persist_attr_done[D == 128][F16][dev]) {
+      if (cudaFuncSetAttribute(ring_fwd_persistent_kernel<D, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return HCP_ERR_CUDA;
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, ring_fwd_persistent_kernel<D, F16>) != cudaSuccess) return HCP_ERR_CUDA;
+      if (2 * 128 * kRegsSoftmaxWide + 128 * kRegsProducerWide > kThreadsWide * fa.numRegs)
+        return HCP_ERR_UNSUPPORTED;
+      int n = 0;
+      if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return HCP_ERR_CUDA;
+      g_sm_count[dev] = n;
+      g_persist_attr_done[D == 128][F16][dev] = true;
+    }
+    sms = g_sm_count[dev];
+  }
+  const int grid = std::min(jobs, sms);
+  ring_fwd_persistent_kernel<D, F16><<<grid, kThreadsWide, smem, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? HCP_OK : HCP_ERR_CUDA;
+}
+
 template <int D, bool F16>
 int launch_fwd(const FwdParams& p, int grid, cudaStream_t st, bool list) {
   // items of more than two segments: the segment-table kernel (mbarrier issuer)
   if (list) return launch_fwd<D, F16, 0, true>(p, grid, st);
   switch (fwd_variant()) {
+    case 7: return launch_fwd_persistent<D, F16>(p, grid, st);
     case 1: return launch_fwd<D, F16, 1>(p, grid, st);
     case 2: return launch_fwd<D, F16, 2>(p, grid, st);
     case 3: return launch_fwd<D, F16, 3>(p, grid, st);
