@@ -38,13 +38,25 @@ def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _same_device(ref: torch.Tensor, **tensors) -> None:
+    """Every given tensor must live on ``ref``'s GPU: the library receives
+    raw addresses, and a host tensor or another GPU's tensor handed to a
+    kernel is a memory fault on the device, not an error the caller sees."""
+    if not ref.is_cuda:
+        raise ValueError("tensors must be CUDA tensors (no CPU path)")
+    idx = ref.get_device()
+    for name, t in tensors.items():
+        if t is not None and (not t.is_cuda or t.get_device() != idx):
+            raise ValueError(f"{name} must be on {ref.device} (got {t.device})")
+
+
 def _dev(t: torch.Tensor):
     """Make the tensor's GPU the current device for the library call: the
     library launches on the current device, into a stream of that device."""
     return torch.cuda.device(t.device)
 
 
-def _ext_sources(ext, dtype):
+def _ext_sources(ext, dtype, ref: torch.Tensor):
     """ctypes array of ``hcp_kv_source`` for a list of (k, v) tensors, each
     [rows, Hkv, D] with its last two dims packed (k and v of one source share
     a row stride), or None."""
@@ -54,8 +66,9 @@ def _ext_sources(ext, dtype):
         raise ValueError(f"at most {C.HCP_MAX_EXT_SOURCES} extra sources per call")
     arr = (C.HcpKvSource * len(ext))()
     for i, (k, v) in enumerate(ext):
-        if k.shape != v.shape or k.dtype != dtype or v.dtype != dtype or not k.is_cuda:
-            raise ValueError(f"extra source {i}: k and v must be CUDA tensors of one shape and q's dtype")
+        if k.shape != v.shape or k.dtype != dtype or v.dtype != dtype:
+            raise ValueError(f"extra source {i}: k and v must be of one shape and q's dtype")
+        _same_device(ref, **{f"ext[{i}].k": k, f"ext[{i}].v": v})
         ks, vs = _rows_heads(k, f"ext[{i}].k"), _rows_heads(v, f"ext[{i}].v")
         if ks != vs:
             raise ValueError(f"extra source {i}: k and v must share a row stride")
@@ -113,6 +126,8 @@ def ring_attn_fwd(
         raise ValueError("q must be a CUDA tensor (no CPU path)")
     if q.dtype not in (torch.bfloat16, torch.float16):
         raise ValueError(f"unsupported dtype {q.dtype}")
+    _same_device(q, k_a=k_a, v_a=v_a, k_b=k_b, v_b=v_b, kv_cache=kv_cache, block_table=block_table, out=out,
+                 lse=lse, merge_o=merge_o, merge_lse=merge_lse)
     num_heads, head_dim = q.shape[1], q.shape[2]
     a = C.HcpFwdArgs()
     a.dtype = _DT[q.dtype]
@@ -170,7 +185,7 @@ def ring_attn_fwd(
         a.merge_o_row_stride = _rows_heads(merge_o, "merge_o")
         a.merge_lse = _ptr(merge_lse)
         a.merge_lse_stride = merge_lse.stride(0)
-    ext_arr = _ext_sources(ext, q.dtype)
+    ext_arr = _ext_sources(ext, q.dtype, q)
     if ext_arr is not None:
         a.ext, a.num_ext = ctypes.cast(ext_arr, ctypes.POINTER(C.HcpKvSource)), len(ext_arr)
     if seg_list is not None:
@@ -231,6 +246,8 @@ def merge_attn_states(
 ) -> None:
     """vLLM ``merge_attn_states`` contract (``hcp_merge_attn_states``): o tensors
     [T, H, D], lse [H, T] float32; writes ``output`` (and ``output_lse``)."""
+    _same_device(output, prefix_output=prefix_output, prefix_lse=prefix_lse, suffix_output=suffix_output,
+                 suffix_lse=suffix_lse, output_lse=output_lse)
     num_tokens, num_heads, head_dim = output.shape
     for t in (prefix_lse, suffix_lse) + ((output_lse,) if output_lse is not None else ()):
         if t.dtype != torch.float32 or t.stride(1) != 1:
@@ -253,6 +270,7 @@ def merge_attn_states_n(output: torch.Tensor, states_o: torch.Tensor, states_lse
     """N-way LSE merge (``hcp_merge_attn_states_n``): states_o [N, T, H, D] and
     states_lse [N, H, T] float32 contiguous -> output [T, H, D] (and output_lse
     [H, T])."""
+    _same_device(output, states_o=states_o, states_lse=states_lse, output_lse=output_lse)
     n, t, h, d = states_o.shape
     if states_o.dtype != torch.float32 or states_lse.dtype != torch.float32:
         raise ValueError("states must be float32")
@@ -293,6 +311,7 @@ def decode_args(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, pee
     the index of its extra source."""
     if not q.is_cuda or q.dtype not in (torch.bfloat16, torch.float16):
         raise ValueError("q must be a bf16/fp16 CUDA tensor (no CPU path)")
+    _same_device(q, peer_k=peer_k, peer_v=peer_v, kv_cache=kv_cache, block_table=block_table, out=out, lse=lse)
     seqs = np.ascontiguousarray(seqs, dtype=np.int32).reshape(-1, DECODE_FIELDS)
     a = C.HcpDecodeArgs()
     a.dtype = _DT[q.dtype]
@@ -323,7 +342,7 @@ def decode_args(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, pee
         a.lse, a.lse_stride = _ptr(lse), lse.stride(0)
     a.seqs = seqs.ctypes.data_as(ctypes.POINTER(C.HcpDecodeSeq))
     a.num_seqs = seqs.shape[0]
-    ext_arr = _ext_sources(ext, q.dtype)
+    ext_arr = _ext_sources(ext, q.dtype, q)
     if ext_arr is not None:
         a.ext, a.num_ext = ctypes.cast(ext_arr, ctypes.POINTER(C.HcpKvSource)), len(ext_arr)
     if peer_src is not None:
@@ -350,6 +369,7 @@ def decode_splitkv(q, seqs, *, scale, num_kv_heads, out, lse=None, peer_k=None, 
     if need < 0:
         raise C.HcpError("hcp_decode_workspace_bytes: invalid arguments")
     ws = workspace if workspace is not None else _workspace(q.device, need)
+    _same_device(q, workspace=ws)
     a.workspace, a.workspace_bytes = _ptr(ws), ws.numel() * ws.element_size()
     with _dev(q):
         C.check(lib.hcp_ring_decode_splitkv(ctypes.byref(a), _stream(q)), "hcp_ring_decode_splitkv")
@@ -365,6 +385,7 @@ def kv_cache_gather(kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
     cache's device.  Returns key, value [n, Hkv, D] (allocated unless given);
     rows of negative or out-of-range slots are zeros.
     """
+    _same_device(kv_cache, slot_mapping=slot_mapping, key=key, value=value)
     if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
         raise ValueError("slot_mapping must be a contiguous int64 tensor")
     if kv_cache.dim() != 4 or not kv_cache.is_contiguous():
@@ -392,6 +413,7 @@ def kv_cache_update(key: torch.Tensor, value: torch.Tensor, kv_cache: torch.Tens
     key/value [n, Hkv, D]; kv_cache [num_blocks, Hkv, block_size, 2*D];
     slot_mapping [n] int64 (negative = padding).
     """
+    _same_device(key, value=value, kv_cache=kv_cache, slot_mapping=slot_mapping)
     if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
         raise ValueError("slot_mapping must be a contiguous int64 tensor")
     if kv_cache.dim() != 4 or not kv_cache.is_contiguous() or kv_cache.dtype != key.dtype:
