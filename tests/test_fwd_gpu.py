@@ -275,6 +275,51 @@ def test_segment_lists_over_separate_chunks(dev):
         P.check_lse(_f(lse[:, qs:qs + L]), want_lse, f"segment list request {r}")
 
 
+def test_many_items_span_several_launches(dev):
+    """More work items (200) and segments (~430) than one launch takes (160
+    and 320): the host splits the call into several launches of one
+    heaviest-first order, and a launch that holds a segment-list item runs
+    the list kernel.  Every request equals the oracle."""
+    from hcp_vllm_plugin_b200 import _capi as C, ops
+    rng = np.random.default_rng(21)
+    g = torch.Generator(device="cpu").manual_seed(21)
+    n = 200
+    tq = rng.integers(1, 41, n)
+    pl = rng.integers(0, 300, n)          # peer keys, contiguous source A, non-causal
+    ll = tq + rng.integers(0, 200, n)     # local keys, contiguous source B, causal
+    qs, ps, ls = (np.concatenate([[0], np.cumsum(x)]).astype(int) for x in (tq, pl, ll))
+    q = torch.randn(int(qs[-1]), H28, D128, generator=g).bfloat16()
+    ka, va = (torch.randn(int(ps[-1]), HKV4, D128, generator=g).bfloat16() for _ in range(2))
+    kb, vb = (torch.randn(int(ls[-1]), HKV4, D128, generator=g).bfloat16() for _ in range(2))
+    items, seg_list = [], []
+    for r in range(n):
+        loc = (C.HCP_SRC_B, int(ls[r]), int(ll[r]), int(ll[r] - tq[r]))  # last query sees every local key
+        if r % 7 == 3 and pl[r] >= 2:    # the peer keys as two segments of a list
+            h = int(pl[r]) // 2
+            seg_list += [(C.HCP_SRC_A, int(ps[r]), h, -1), (C.HCP_SRC_A, int(ps[r]) + h, int(pl[r]) - h, -1), loc]
+            items.append((int(qs[r]), int(tq[r]), 0, int(qs[r]), (C.HCP_SRC_LIST, len(seg_list) - 3, 3, 0), None))
+        else:
+            peer = (C.HCP_SRC_A, int(ps[r]), int(pl[r]), -1) if pl[r] else None
+            items.append((int(qs[r]), int(tq[r]), 0, int(qs[r]), peer, loc))
+    assert len(items) > 160 and sum(3 if it[4] and it[4][0] == C.HCP_SRC_LIST else 2 for it in items) > 320
+    qd = q.to(dev)
+    out = torch.zeros_like(qd)
+    lse = torch.zeros(H28, qd.shape[0], dtype=torch.float32, device=dev)
+    ops.ring_attn_fwd(qd, ops.make_work(items), scale=D128 ** -0.5, num_kv_heads=HKV4, out=out, lse=lse,
+                      k_a=ka.to(dev), v_a=va.to(dev), k_b=kb.to(dev), v_b=vb.to(dev), seg_list=np.array(seg_list))
+    torch.cuda.synchronize()
+    got, got_lse = _f(out), _f(lse)
+    for r in range(n):
+        qr = _f(q[qs[r]:qs[r + 1]])
+        want, want_lse = ro.attn_with_lse(qr, _f(kb[ls[r]:ls[r + 1]]), _f(vb[ls[r]:ls[r + 1]]), D128 ** -0.5,
+                                          int(ll[r] - tq[r]))
+        if pl[r]:
+            o_p, l_p = ro.attn_with_lse(qr, _f(ka[ps[r]:ps[r + 1]]), _f(va[ps[r]:ps[r + 1]]), D128 ** -0.5, None)
+            want, want_lse = ro.merge_pair(want, want_lse, o_p, l_p)
+        P.check_out(got[qs[r]:qs[r + 1]], want, f"request {r} of 200")
+        P.check_lse(got_lse[:, qs[r]:qs[r + 1]], want_lse, f"request {r} of 200")
+
+
 @pytest.mark.parametrize("tq,tk,off,window", [
     (1000, 1000, 0, 1), (1000, 1000, 0, 100), (1000, 1000, 0, 200), (1000, 1000, 0, 700),
     (300, 2000, 1700, 333), (1, 4096, 4095, 129), (513, 513, 0, 128)])
