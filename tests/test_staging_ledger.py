@@ -113,3 +113,43 @@ def test_layer_feed_stop_ends_a_waiting_thread():
     feed.wait("l.layers.0.x")
     feed.stop()                         # blocked on the window: returns without staging the rest
     assert feed.error is None
+
+
+def test_chunk_ledger_random_holds_and_releases_follow_a_count_model():
+    """500 random holds and releases over 12 requests sharing 6 chunks: a
+    chunk stays staged exactly while some request that holds it is in flight,
+    the backend's request map holds exactly the live requests, and
+    ``release_all`` leaves nothing staged."""
+    import random
+
+    rnd = random.Random(5)
+    led = ChunkLedger()
+    chunks = [f"c{i}" for i in range(6)]
+    layer = "model.layers.0.attn"
+    live: dict = {}  # request -> (first block id, chunks)
+    for step in range(500):
+        rid = f"r{rnd.randrange(12)}"
+        if rid in live and rnd.random() < 0.6:
+            assert led.release(rid)
+            del live[rid]
+        elif rid not in live:
+            held = rnd.sample(chunks, rnd.randint(1, 4))
+            for ck in held:  # the connector stages a chunk before a request holds it
+                if (ck, layer) not in rb.PEER_KV_STAGING:
+                    _stage(ck, layer)
+            fb = 1000 + step
+            led.hold(rid, fb, held)
+            live[rid] = (fb, held)
+        want = {}
+        for _, held in live.values():
+            for ck in held:
+                want[ck] = want.get(ck, 0) + 1
+        assert led.holder_counts() == want
+        staged = {ck for ck, _ in rb.PEER_KV_STAGING}
+        # every chunk here is held as soon as it is staged, so staged == held
+        assert set(want) <= staged, "a chunk was dropped while a request still held it"
+        assert staged <= set(want), "a chunk stayed staged after its last holder left"
+        assert sorted(led.requests()) == sorted(live)
+        assert {fb: list(h) for fb, h in live.values()} == dict(rb.PEER_REQ_MAP)
+    led.release_all()
+    assert not rb.PEER_KV_STAGING and not rb.PEER_REQ_MAP and led.holder_counts() == {}
