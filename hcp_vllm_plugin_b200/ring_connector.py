@@ -484,6 +484,12 @@ class HcpRingKvConnector(KVConnectorBase_V1):
         if device.type == "cuda" and self._side_stream is None:
             self._side_stream = torch.cuda.Stream(device=device)
         for req in need:
+            if req.req_id in self._feeds or req.req_id in self._ledger.requests() or \
+                    req.req_id in self._slots.holders():
+                # loaded again (a request resumed after preemption is
+                # rescheduled from its prefill): the new registration replaces
+                # the old one, whose chunk holds and ring slot are returned
+                self._end_request(req.req_id)
             expected = align_down(req.prefix_len or self._prefix_len, self._block_size)
             if self._decode_owner:
                 self._register_decode(req, expected, device)   # may fail: before any other state

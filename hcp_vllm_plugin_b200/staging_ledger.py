@@ -191,6 +191,9 @@ class DecodeSlotPool:
         self._taken: dict[str, tuple[int, int]] = {}   # req -> (slot, first block id)
 
     def take(self, req_id: str, first_block_id: int) -> int:
+        if req_id in self._taken:
+            raise RuntimeError(f"HcpRingKvConnector: request {req_id} already holds decode ring slot "
+                               f"{self._taken[req_id][0]}")
         if not self.free:
             raise RuntimeError(f"HcpRingKvConnector: all {self.slots} decode ring slots are in use "
                                "(ring_decode_slots)")

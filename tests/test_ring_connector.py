@@ -523,3 +523,32 @@ def test_decode_ring_slots_exhausted(tmp_path):
         conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in _layers(2)}))
     assert conn._ledger.requests() == ["r0"] and 2 not in rb.PEER_REQ_MAP   # r1 left no state behind
     conn.shutdown()
+
+
+def test_a_request_loaded_again_replaces_its_registration(tmp_path):
+    """A request the scheduler hands the worker again while it is still
+    registered (resumed after preemption, it is rescheduled from its
+    prefill, with new blocks): its old chunk holds, backend mapping and
+    decode-ring slot are returned before the new ones are taken, so nothing
+    leaks and the step does not fail."""
+    from hcp_vllm_plugin_b200 import ring_backend as rb
+
+    STORES.clear()
+    STORES["c0"] = torch.randn(2, 2, 16, 2, 8)
+    _write_marker(str(tmp_path), "c0", STORES["c0"])
+    conn = _consumer(str(tmp_path), 2, dict(OWNER, ring_decode_slots=2))
+    names = _layers(2)
+    conn.bind_connector_metadata(_load_meta([("r0", 4, ["c0"], 16)]))
+    conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in names}))
+    for name in names:
+        conn.wait_for_layer_load(name)
+    conn.bind_connector_metadata(_load_meta([("r0", 8, ["c0"], 16)]))   # the same request, new blocks
+    conn.start_load_kv(fk.forward_context({n: torch.empty(0) for n in names}))
+    for name in names:
+        conn.wait_for_layer_load(name)
+    assert rb.PEER_REQ_MAP == {8: ["c0"]} and list(rb.DECODE_RING_MAP) == [8]
+    assert conn._ledger.holder_counts() == {"c0": 1} and conn._slots.holders() == ["r0"]
+    assert len(conn._slots.free) == 1                    # one slot in use, none leaked
+    conn.get_finished({"r0"})
+    assert rb.PEER_REQ_MAP == {} and rb.DECODE_RING_MAP == {} and len(conn._slots.free) == 2
+    conn.shutdown()

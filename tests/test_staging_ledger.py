@@ -153,3 +153,11 @@ def test_chunk_ledger_random_holds_and_releases_follow_a_count_model():
         assert {fb: list(h) for fb, h in live.values()} == dict(rb.PEER_REQ_MAP)
     led.release_all()
     assert not rb.PEER_KV_STAGING and not rb.PEER_REQ_MAP and led.holder_counts() == {}
+
+
+def test_decode_slot_pool_refuses_a_second_slot_for_one_request():
+    pool = DecodeSlotPool(3)
+    assert pool.take("r1", 5) == 0
+    with pytest.raises(RuntimeError, match="already holds decode ring slot 0"):
+        pool.take("r1", 6)
+    assert pool.holders() == ["r1"] and list(pool.free) == [1, 2]
