@@ -294,8 +294,11 @@ _workspaces: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Cached device scratch (grown on demand) for the split-KV partials."""
-    key = (device.type, device.index)
+    """Cached device scratch (grown on demand) for the split-KV partials, one
+    per stream: calls on one stream run in order, while the decode ring's
+    serve thread and the backend decode on different streams of one device
+    at the same time and must not share partials."""
+    key = (device.type, device.index, torch.cuda.current_stream(device).cuda_stream)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)

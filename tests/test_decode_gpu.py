@@ -138,3 +138,38 @@ def test_kv_cache_update_matches_oracle(dev):
     want = _f(cache)
     ro.kv_cache_update(want, _f(key), _f(val), slots.numpy())
     np.testing.assert_array_equal(_f(dc), want)
+
+
+def test_decode_on_two_streams_keeps_each_streams_partials(dev):
+    """The decode ring's serve thread and the backend run split-KV decode on
+    different streams of one device at the same time: each stream's calls
+    use their own cached workspace, so results launched back to back on two
+    streams equal the same calls run one after the other, bit for bit."""
+    from hcp_vllm_plugin_b200 import ops
+    g = torch.Generator(device=dev).manual_seed(3)
+    H, HKV, D, n, keys = 28, 4, 128, 8, 8192
+
+    def problem():
+        q = torch.randn(n, H, D, generator=g, device=dev, dtype=torch.bfloat16)
+        pk = torch.randn(n * keys, HKV, D, generator=g, device=dev, dtype=torch.bfloat16)
+        pv = torch.randn(n * keys, HKV, D, generator=g, device=dev, dtype=torch.bfloat16)
+        return q, pk, pv, np.array([(i, i * keys, keys, -1, 0, 0) for i in range(n)], np.int32)
+
+    def run(q, pk, pv, seqs):
+        out = torch.empty_like(q)
+        lse = torch.empty(H, n, dtype=torch.float32, device=dev)
+        ops.decode_splitkv(q, seqs, scale=D ** -0.5, num_kv_heads=HKV, out=out, lse=lse, peer_k=pk, peer_v=pv)
+        return out, lse
+
+    probs = [problem(), problem()]
+    serial = [run(*p) for p in probs]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    for _ in range(5):
+        res = []
+        for s, p in zip(streams, probs):
+            with torch.cuda.stream(s):
+                res.append(run(*p))
+        torch.cuda.synchronize()
+        for (o, l), (so, sl) in zip(res, serial):
+            assert torch.equal(o, so) and torch.equal(l, sl)
